@@ -1,0 +1,483 @@
+"""Benchmark: LSA decode select+read at 32k context, bf16, on B200.
+
+Workload ("decode32k"): B=1, one query token, Hq=32, Hkv=8, Dh=128, bf16, drift keys,
+64-token buckets in 512-token cluster blocks (8 per block, cap 128, pools of 4), top-32
+buckets (2048-token budget), window 64, sinks 4 - the D-LSA Flat arm through the fused
+select (LSA_SELECT_IMPL=fused: one launch from index query to read lists) and the split-K
+TMA-gather read. A STEP is one decoded token through LAYERS = 32 layers, each layer its
+own independent 32k KV cache (4.3 GB of K/V in all), so one step touches 32 x ~9.7 MB,
+more than twice the 126 MB L2, before any cache is revisited: no L2 flush is needed.
+The select+read index (buckets) is built before timing, as in the reference's bench
+(src/lsa_rocm_lab/port/bench.py:113-154 times select+read on a prebuilt index).
+
+value = algorithmic bytes of the step / step time, in GB/s (whole job: summed over the
+N replica ranks, max time over ranks); us_per_select_read = step time / LAYERS. The
+device-timed region replays one CUDA graph of the K steps' kernels with inputs resident.
+``e2e`` is the same metric through the public Python API with host buffers: every step
+copies the 32 layers' query rows from pinned host memory, runs make_index_space +
+flat_select + lsa_read per layer, and copies the outputs back.
+
+``--impl reference`` times the reference's CPU path for this workload on the host cores:
+the CPU checker (oracle/, a restatement of the reference's select + read; the reference's
+own path needs the absent upstream package and a ROCm GPU) over a bounded sample of
+select+reads per step, with one worker process per core.
+
+Multi-GPU (--gpus N under torchrun): the decode of one sequence does not shard, so the N
+ranks run independent replicas (scaling "weak"); no collective is on the data path.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PKG = ROOT / "latent-sparse-attention-rocm_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "decode select+read µs/step & HBM GB/s @32k bf16; prefill select+read tok/s vs dense"
+T_CTX, HQ, HKV, DH = 32768, 32, 8, 128
+LAYERS = 32
+CFG = dict(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap=128, top_p=32, top_k=2048,
+           window_size=64, sink_size=4)
+SEED = 20261105
+
+
+def _load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _traffic_from_profile(name: str):
+    """dram bytes per launch recorded in the committed ncu summary (profiles/), else None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------------------- B200 arm
+
+
+def build_layers(dev, lsa):
+    """LAYERS independent caches: K/V, the decode row's q and index query, the Ward buckets."""
+    import torch
+
+    from lsa_b200.index_space import regroup_rows
+    from lsa_b200.synthetic import drift_keys
+
+    pcfg = lsa.PortConfig(**CFG)
+    layers = []
+    for layer in range(LAYERS):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(SEED + T_CTX + layer)
+        k = drift_keys(T_CTX, HKV, DH, gen, dev).to(torch.bfloat16)
+        v = torch.randn(1, T_CTX, HKV, DH, generator=gen, device=dev).to(torch.bfloat16)
+        q = torch.randn(1, 1, HQ, DH, generator=gen, device=dev).to(torch.bfloat16)
+        _, ik = regroup_rows(k[0], k[0])  # index keys (the query half of this call is unused)
+        buckets = lsa.build_buckets_gpu(ik, pcfg)
+        del ik
+        iq, _ = regroup_rows(q[0], k[0, -1:])
+        layers.append(dict(k=k, v=v, q=q, iq=iq.to(torch.bfloat16), buckets=buckets,
+                           pos=torch.tensor([T_CTX - 1], device=dev, dtype=torch.int32)))
+    torch.cuda.synchronize(dev)
+    return pcfg, layers
+
+
+def run_b200(args, rank, world, dev):
+    import torch
+
+    import lsa_b200 as lsa
+    from lsa_b200 import pipeline
+
+    os.environ["LSA_SELECT_IMPL"] = "fused"
+    scale = DH ** -0.5
+    pcfg, layers = build_layers(dev, lsa)
+    stream = torch.cuda.Stream(dev)
+
+    def select(L):
+        return pipeline._select_fused(L["iq"], L["pos"], L["buckets"], pcfg, pcfg.top_k, "bf16")
+
+    def read(L, lists, lengths):
+        return lsa.lsa_read(L["q"], L["k"], L["v"], lists[None], lengths[None], scale)
+
+    def step():
+        outs = []
+        for L in layers:
+            lists, lengths = select(L)
+            outs.append(read(L, lists, lengths))
+        return outs
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+        sel = [select(L) for L in layers]
+        stream.synchronize()
+    lengths_all = [int(s[1].item()) for s in sel]
+    n_ids = sum(lengths_all)
+    members_bytes = LAYERS * CFG["top_p"] * CFG["bucket_cap"] * 4
+    visible = min((T_CTX - 1) // CFG["cluster_block_size"] * (CFG["cluster_block_size"] // CFG["bucket_size"]),
+                  layers[0]["buckets"].rows)
+    centroid_bytes = LAYERS * visible * HKV * DH * 2
+    kv_bytes = n_ids * HKV * DH * 2 * 2
+    small = LAYERS * (HQ * DH * 2 * 2 + HKV * DH * 2 + (CFG["top_k"] + CFG["window_size"] + CFG["sink_size"]) * 4 * 2)
+    step_bytes = centroid_bytes + members_bytes + kv_bytes + small
+    read_bytes_per_launch = (kv_bytes + n_ids * 4) / LAYERS + HQ * DH * 2 * 2
+
+    # one graph holding K steps (LAYERS select+read pairs each)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.steps):
+            step()
+    read_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(read_graph, stream=stream):
+        for _ in range(args.steps):
+            for L, (ls, ln) in zip(layers, sel):
+                read(L, ls, ln)
+    select_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(select_graph, stream=stream):
+        for _ in range(args.steps):
+            for L in layers:
+                select(L)
+
+    def timed(g, reps=1):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            stream.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize(dev)
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+            stream.synchronize()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        return ev0.elapsed_time(ev1) / reps
+
+    with ClockSampler(dev.index) as clocks:
+        ms_total = timed(graph)
+    ms_read = timed(read_graph)
+    ms_select = timed(select_graph)
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_per_step = ms_total / args.steps
+    value = world * step_bytes / (ms_per_step / 1e3) / 1e9
+    us_read = ms_read / args.steps / LAYERS * 1e3
+    us_select = ms_select / args.steps / LAYERS * 1e3
+
+    # end to end through the public API with host buffers
+    q_host = torch.stack([L["q"] for L in layers]).cpu().pin_memory()
+    k_last = [L["k"][0, -1:] for L in layers]
+    out_host = torch.empty(LAYERS, 1, 1, HQ, DH, dtype=torch.bfloat16).pin_memory()
+    from lsa_b200.index_space import regroup_rows
+
+    def e2e_step():
+        qd = q_host.to(dev, non_blocking=True)
+        outs = []
+        for i, L in enumerate(layers):
+            iq, _ = regroup_rows(qd[i, 0], k_last[i])
+            lists, lengths = lsa.flat_select(iq, L["pos"], L["buckets"], pcfg)
+            outs.append(lsa.lsa_read(qd[i], L["k"], L["v"], lists[None], lengths[None], scale))
+        out_host.copy_(torch.stack(outs), non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+        stream.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        ev1.record(stream)
+        stream.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # dense decode baseline (SDPA over the whole cache) on the same rotation
+    dense_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for L in layers:
+            lsa.dense_read(L["q"], L["k"], L["v"], scale)
+        stream.synchronize()
+    with torch.cuda.graph(dense_graph, stream=stream):
+        for L in layers:
+            lsa.dense_read(L["q"], L["k"], L["v"], scale)
+    us_dense = timed(dense_graph, reps=2) / LAYERS * 1e3
+
+    hbm, tflops, peak_kind = _load_peaks()
+    read_gbs = read_bytes_per_launch / (us_read * 1e-6) / 1e9
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded drift keys, N(0,1) q/v)",
+        "config": {"workload": "decode32k", "layers_per_step": LAYERS, "context": T_CTX, "batch": 1,
+                   "heads_q": HQ, "heads_kv": HKV, "head_dim": DH, "bucket_size": CFG["bucket_size"],
+                   "top_p_buckets": CFG["top_p"], "budget_tokens": CFG["top_k"], "window": CFG["window_size"],
+                   "sink": CFG["sink_size"], "select_impl": "fused", "parallelism": f"replicas{world}",
+                   "l2": "no flush: 32 independent 32k caches, each step touches 32 x ~9.7 MB > 2x L2"},
+        "us_per_select_read": round(ms_per_step / LAYERS * 1e3, 3),
+        "us_per_select": round(us_select, 3), "us_per_read": round(us_read, 3),
+        "dense_us_per_decode": round(us_dense, 3),
+        "speedup_vs_dense_decode": round(us_dense / (ms_per_step / LAYERS * 1e3), 3),
+        "bytes_per_step": step_bytes, "keys_read_per_step": n_ids,
+        "gpu_launches": args.steps * LAYERS * 2,
+        "roofline": {"bound": "hbm", "kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(read_gbs / hbm, 4), "peak_kind": peak_kind,
+                     "traffic": _traffic_from_profile("sparse_read_decode32k.md"),
+                     "bytes_per_launch": round(read_bytes_per_launch)},
+        "step_roofline_frac": round(value / world / hbm, 4),
+        "e2e": {"value": round(world * step_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(q_host.numel() * 2),
+                "d2h_bytes_per_step": int(out_host.numel() * 2)},
+        "clocks": clocks.summary(),
+    }
+    return result, layers
+
+
+# --------------------------------------------------------------------------- CPU baseline
+
+
+def _cpu_sample(payload):
+    """One worker: time select+read on the checker for `n` decode rows of one cache."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    path, n = payload
+    blob = np.load(path)
+    ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
+    cfg = O.Config(**CFG)
+    t0 = time.perf_counter()
+    length = 0
+    for _ in range(n):
+        lists, lengths = O.flat_select(blob["iq"], np.array([T_CTX - 1]), ob, cfg)
+        O.sparse_read(blob["q"], blob["k"], blob["v"], lists[None], lengths[None], DH ** -0.5)
+        length = int(lengths[0])
+    return time.perf_counter() - t0, n, length
+
+
+def _dump_layer_for_cpu(L, path):
+    import numpy as np
+
+    b = L["buckets"]
+    np.savez(path, cf=b.centroids_f32.cpu().numpy(), cb=b.centroids.float().cpu().numpy(),
+             members=b.members.cpu().numpy(), sizes=b.sizes.cpu().numpy(), sums=b.key_sums.cpu().numpy(),
+             iq=L["iq"].float().cpu().numpy(), q=L["q"].float().cpu().numpy(), k=L["k"].float().cpu().numpy(),
+             v=L["v"].float().cpu().numpy())
+
+
+def _bytes_per_select_read(length: int) -> int:
+    """Algorithmic bytes of one decode select+read (same count as the B200 arm's step / LAYERS)."""
+    visible = (T_CTX - 1) // CFG["cluster_block_size"] * (CFG["cluster_block_size"] // CFG["bucket_size"])
+    width = CFG["top_k"] + CFG["window_size"] + CFG["sink_size"]
+    return (visible * HKV * DH * 2 + CFG["top_p"] * CFG["bucket_cap"] * 4 + length * HKV * DH * 2 * 2
+            + HQ * DH * 2 * 2 + HKV * DH * 2 + width * 4 * 2)
+
+
+def cpu_baseline(layer, seconds=10.0):
+    """The checker's select+read on this box's host, single core: a bounded sample."""
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "layer0.npz")
+        _dump_layer_for_cpu(layer, path)
+        dt, n, _ = _cpu_sample((path, 1))
+        reps = max(1, min(64, int(seconds / max(dt, 1e-3))))
+        dt, n, length = _cpu_sample((path, reps))
+    per = dt / n
+    return {"value": round(_bytes_per_select_read(length) / per / 1e9, 4), "unit": "GB/s", "cores": 1,
+            "kind": "port",
+            "sample": f"{n} decode select+read on one 32k cache (oracle/, C + numpy), {per * 1e3:.2f} ms each"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU path of the reference for this workload, all host cores.
+
+    The index is built on the GPU when one is visible (bit-identical to the checker's own
+    build, which the parity tests pin), else by the checker; only select+read is timed."""
+    if rank != 0:
+        return None
+    import multiprocessing as mp
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    cores = os.cpu_count() or 1
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "layer0.npz")
+        if torch.cuda.is_available():
+            import lsa_b200 as lsa
+            from lsa_b200.index_space import regroup_rows
+            from lsa_b200.synthetic import drift_keys
+
+            dev = torch.device("cuda:0")
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(SEED + T_CTX)
+            k = drift_keys(T_CTX, HKV, DH, gen, dev).to(torch.bfloat16)
+            v = torch.randn(1, T_CTX, HKV, DH, generator=gen, device=dev).to(torch.bfloat16)
+            q = torch.randn(1, 1, HQ, DH, generator=gen, device=dev).to(torch.bfloat16)
+            _, ik = regroup_rows(k[0], k[0])
+            buckets = lsa.build_buckets_gpu(ik, lsa.PortConfig(**CFG))
+            iq, _ = regroup_rows(q[0], k[0, -1:])
+            _dump_layer_for_cpu(dict(k=k, v=v, q=q, iq=iq.to(torch.bfloat16), buckets=buckets), path)
+        else:
+            from oracle import oracle as O
+
+            g = np.random.default_rng(SEED)
+            kk = O.bf16_round(g.standard_normal((T_CTX, HKV, DH)).astype(np.float32))
+            qq = O.bf16_round(g.standard_normal((1, HQ, DH)).astype(np.float32))
+            _, ik = O.regroup(kk, kk)
+            ob = O.build_buckets(ik, O.Config(**CFG))
+            iq, _ = O.regroup(qq, kk[-1:])
+            np.savez(path, cf=ob.centroids_f32, cb=ob.centroids_bf16, members=ob.members, sizes=ob.sizes,
+                     sums=ob.key_sums, iq=O.bf16_round(iq), q=qq[None], k=kk[None],
+                     v=O.bf16_round(g.standard_normal((1, T_CTX, HKV, DH)).astype(np.float32)))
+        dt1, _, length = _cpu_sample((path, 1))
+        per_worker = max(1, int(2.0 / max(dt1, 1e-3)))  # about 2 s of work per worker per step
+        ctx = mp.get_context("spawn")
+        with ctx.Pool(cores) as pool:
+            samples = []
+            for i in range(args.warmup + args.steps):
+                t0 = time.perf_counter()
+                res = pool.map(_cpu_sample, [(path, per_worker)] * cores)
+                wall = time.perf_counter() - t0
+                if i >= args.warmup:
+                    samples.append((wall, sum(r[1] for r in res)))
+    wall = sum(w for w, _ in samples)
+    n_sr = sum(n for _, n in samples)
+    value = n_sr * _bytes_per_select_read(length) / wall / 1e9
+    ms_per_step = wall / len(samples) * 1e3
+    return {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)", "config": {"workload": "decode32k", "select_impl": "reference-cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{per_worker} decode select+read per worker per step, {cores} spawn "
+                                       "workers, oracle/ (C + numpy)"},
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+# --------------------------------------------------------------------------- main
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    import torch
+
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return 0
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    result, layers = run_b200(args, rank, world, dev)
+    if rank == 0:
+        if not args.no_cpu_baseline and world == 1:
+            result["cpu_baseline"] = cpu_baseline(layers[0])
+        else:
+            result["cpu_baseline"] = None
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

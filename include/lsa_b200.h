@@ -1,0 +1,157 @@
+/*
+ * lsa_b200.h - C ABI of the B200 (sm_100a) Latent Sparse Attention select + read kernels.
+ *
+ * Library: latent-sparse-attention-rocm_b200/lsa_b200/liblsa_b200.so (built by
+ * latent-sparse-attention-rocm_b200/build.py). Every entry point takes plain device
+ * pointers, sizes and a cudaStream_t, launches asynchronously on that stream and
+ * returns a status: LSA_OK, or LSA_ERR_ARG for rejected arguments, LSA_ERR_CUDA for a
+ * failed launch. Kernels that wait on the device bound every wait and record
+ * LSA_ERR_TIMEOUT in a device status word instead of hanging; the bucket builds record
+ * LSA_ERR_SHORT there when a block cannot reach its bucket count under the cap.
+ *
+ * Dtype codes: 0 = fp32, 1 = fp16, 2 = bf16. "Counters" arguments are int32 device
+ * arrays that must be zero before the call; the kernels leave them zero, so one
+ * buffer serves every later call on the same stream (and CUDA-graph replays).
+ * Calls sharing a scratch or counters buffer must not overlap on the GPU.
+ *
+ * Each declaration names the reference interface it replaces: AIwork4me/
+ * latent-sparse-attention-rocm, file:line inside that project.
+ */
+#ifndef LSA_B200_H
+#define LSA_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LSA_OK 0
+#define LSA_ERR_ARG (-1)
+#define LSA_ERR_CUDA (-2)
+#define LSA_ERR_TIMEOUT (-3)
+#define LSA_ERR_SHORT (-4)
+
+/* ---------------------------------------------------------------- index space */
+
+/* make_index_space -> upstream regroup (src/lsa_rocm_lab/port/gates.py:50-59).
+ * q [T, Hq, D], k [T, Hkv, D] (dtype) -> index queries / unit index keys [T, Hkv*D] fp32. */
+int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, float* iq,
+                float* ik, cudaStream_t stream);
+
+/* F.normalize of each row (pipeline.py:113, :179), optional bf16 copy (round to nearest even). */
+int lsa_normalize_rows(const float* x, int64_t n, int64_t d, float* out, void* out_bf16, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- bucket build */
+
+int64_t lsa_build_buckets_workspace(int64_t T, int64_t d, int64_t block, int64_t pool);
+
+/* build_buckets_gpu (src/lsa_rocm_lab/port/pipeline.py:71-116): pools, spherical Ward merge
+ * (upstream triton_ward.ward_merge, :97), members (bucket_members_from_labels, :101) and
+ * centroids (:108-114) of the T / block closed blocks. keys [T, d] fp32; outputs
+ * centroids_f32 / centroids_bf16 [rows, d], members [rows, cap] int32 (-1 padded),
+ * sizes [rows], key_sums [rows, d] fp32; rows = (T / block) * bpb. status: device int32. */
+int lsa_build_buckets(const float* keys, int64_t T, int64_t d, int64_t block, int64_t pool, int64_t bpb, int64_t cap,
+                      float* centroids_f32, void* centroids_bf16, int32_t* members, int32_t* sizes, float* key_sums,
+                      void* workspace, int64_t workspace_bytes, int32_t* status, cudaStream_t stream);
+
+/* position_buckets (pipeline.py:378-403): runs of bucket_size consecutive keys. */
+int lsa_position_buckets(const float* keys, int64_t T, int64_t d, int64_t block, int64_t bucket_size, int64_t cap,
+                         float* centroids_f32, void* centroids_bf16, int32_t* members, int32_t* sizes,
+                         float* key_sums, int32_t* status, cudaStream_t stream);
+
+int64_t lsa_pair_to_size_workspace(int64_t blocks, int64_t n, int64_t d);
+
+/* _pair_to_size (pipeline.py:136-150; upstream cluster_node_buckets iterated): log2(size)
+ * halvings of each block of n rows. labels [blocks, n], order [blocks * n] int64 (rows in
+ * node order, the children table of build_hierarchy_gpu, :173-179), node_sums. */
+int lsa_pair_to_size(const float* sums, int64_t blocks, int64_t n, int64_t d, int64_t size, int32_t* labels,
+                     int64_t* order, float* node_sums, void* workspace, int64_t workspace_bytes, int32_t* status,
+                     cudaStream_t stream);
+
+/* ---------------------------------------------------------------- select */
+
+/* _production_scores (pipeline.py:217-232): scores [R, N] fp32 = canonical fp32 dot of each
+ * query row with each centroid. (q, c) dtypes: (bf16, bf16), (fp32, fp32), (fp32, bf16). */
+int lsa_bucket_scores(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                      int64_t N, int64_t d, float* scores, int64_t lds, cudaStream_t stream);
+
+/* visible_counts (pipeline.py:184-186): min(rows, pos / block * bpb). */
+int lsa_visible_counts(const int32_t* positions, int64_t R, int64_t block, int64_t bpb, int64_t rows, int32_t* counts,
+                       cudaStream_t stream);
+
+/* The listing, whole path (upstream TopK.listed, pipeline.py:266-267): every column packed
+ * (ordered_bits(score) << 32 | 0x7FFFFFFF - col), EMPTY (INT64_MIN) at or past lengths[r]. */
+int lsa_pack_keys(const float* scores, int64_t R, int64_t N, int64_t lds, const int32_t* lengths, int64_t* keys,
+                  int64_t ldk, cudaStream_t stream);
+
+/* best_first_keys (pipeline.py:189-214): slots >= counts[r] masked EMPTY (counts may be
+ * NULL), the k greatest keys sorted descending into out [R, ldo]. */
+int lsa_best_first_keys(const int64_t* keys, int64_t R, int64_t N, int64_t ldk, int64_t k, const int32_t* counts,
+                        int64_t* out, int64_t ldo, cudaStream_t stream);
+
+/* upstream keys.unpack_ids (pipeline.py:268): key -> bucket id, EMPTY -> -1. */
+int lsa_unpack_ids(const int64_t* keys, int64_t n, int32_t* ids, cudaStream_t stream);
+
+/* select_fused.select_topk_scores (src/lsa_rocm_lab/port/select_fused.py:83-137): scores ->
+ * the min(top_p, N) greatest packed keys of the live columns, sorted, EMPTY tail to ldo. */
+int lsa_select_topk_scores(const float* scores, int64_t R, int64_t N, int64_t lds, const int32_t* lengths,
+                           int64_t top_p, int64_t* out, int64_t ldo, cudaStream_t stream);
+
+/* upstream expansion.expand_in_order (pipeline.py:269-271): picked bucket ids [R, P] (-1 =
+ * none) -> read lists [R, top_k + window + sink] (-1 padded) and lengths [R]. */
+int lsa_expand_in_order(const int32_t* picked, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
+                        int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                        int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream);
+
+/* select_fused.expand_in_order_from_keys (select_fused.py:217-280): the walk reading packed keys. */
+int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk, const int32_t* members,
+                         int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                         int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream);
+
+int64_t lsa_select_fused_scratch(int64_t R, int64_t N);
+
+/* flat_select with LSA_SELECT_IMPL=fused (pipeline.py:274-316): ONE launch from index queries
+ * to read lists - scoring over many CTAs, the last CTA of a row sorts and expands.
+ * counters: R int32. max_position < 0: size the grid for every column. */
+int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                     int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
+                     int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
+                     int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                     int64_t max_position, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- tree */
+
+int lsa_tree_plan(int64_t R, int64_t n_built, const int64_t* level_counts, int64_t beam, int64_t size, int64_t nb,
+                  int64_t bpb, int64_t top_p, int64_t* scratch_bytes, int64_t* n_counters);
+
+/* tree_select (pipeline.py:319-337; src/lsa_rocm_lab/port/_tree.py:318-373 beam,
+ * :100-142 growth): picks [R, top_p] int32 (-1 padded). level_centroids, level_children
+ * and level_counts are HOST arrays of n_built device pointers / node counts. */
+int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                    int64_t rows, int64_t n_built, const float* const* level_centroids,
+                    const int64_t* const* level_children, const int64_t* level_counts, const float* bucket_centroids,
+                    int64_t size, int64_t nb, int64_t top_level, int64_t beam, int64_t top_p, int32_t* picks,
+                    void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream);
+
+/* ---------------------------------------------------------------- read */
+
+/* Split plan of lsa_sparse_read: splits per (row, KV head), scratch bytes, counters (the
+ * last counter is the status word). splits_req <= 0 chooses from the SM count. */
+int lsa_sparse_read_plan(int64_t B, int64_t Tq, int64_t Hq, int64_t Hkv, int64_t D, int64_t width, int64_t splits_req,
+                         int64_t* splits, int64_t* scratch_bytes, int64_t* n_counters);
+
+/* sparse_read / sparse_read_tiled / sparse_read_auto (src/lsa_rocm_lab/port/read_kernel.py:80-120,
+ * read_kernel_tiled.py:92-156): q [B, Tq, Hq, D], k/v [B, Tk, Hkv, D] (dtype, D in {64, 128},
+ * Hq / Hkv <= 8), ids [B*Tq, width] int32, lengths [B*Tq] int32 -> out like q. */
+int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
+                    const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D,
+                    int64_t width, float scale, void* out, void* scratch, int64_t scratch_bytes, int32_t* counters,
+                    int64_t n_counters, int64_t splits, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LSA_B200_H */

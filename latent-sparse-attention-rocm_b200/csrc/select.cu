@@ -1,0 +1,469 @@
+// select.cu - bucket scoring, packed-key top-k and the rank-order expansion (sm_100a).
+//
+// Reference (AIwork4me/latent-sparse-attention-rocm, paths inside that project):
+//   scores            src/lsa_rocm_lab/port/pipeline.py:217-232 (_production_scores)
+//   listing + top-k   pipeline.py:189-214, 248-271; select_fused.py:52-137
+//   expansion walk    select_fused.py:140-280 (upstream _expand_in_order semantics)
+//
+// Three arms, byte-identical by construction (LSA_SELECT_IMPL):
+//   reference    : scores -> pack (listing) -> best-first top-k -> unpack -> expand
+//   fused_unpack : scores -> pack -> best-first top-k -> expand reading the keys
+//   fused        : ONE launch from index queries to read lists: every CTA scores a slice
+//                  of the visible buckets, the last CTA of a row (atomic ticket) sorts the
+//                  row's packed keys and walks the expansion.
+#include "common.cuh"
+
+namespace lsa {
+
+constexpr int kSortCap = 8192;  // keys sorted in one shared-memory pass (64 KB)
+
+// ------------------------------------------------------------------ scoring
+
+// scores[r, n] = cdot(q_r, c_n) for n < N. One warp per column; the query row's lane
+// chunks stay in registers for all the CTA's columns.
+template <typename TQ, typename TC, int CHUNKS>
+__global__ void __launch_bounds__(256) scores_kernel(const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c,
+                                                     int64_t N, int d, float* __restrict__ out, int64_t ldo,
+                                                     int cols_per_cta) {
+    int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int nchunks = d >> 3;
+    float x[CHUNKS][8];
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        int ch = lane + 32 * j;
+        if (ch < nchunks) load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+    }
+    int64_t c0 = (int64_t)blockIdx.x * cols_per_cta;
+    int64_t c1 = min(c0 + cols_per_cta, N);
+    for (int64_t n = c0 + warp; n < c1; n += blockDim.x >> 5) {
+        float p = lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks);
+        p = butterfly_sum(p);
+        if (lane == 0) out[r * ldo + n] = p;
+    }
+}
+
+__global__ void visible_counts_kernel(const int32_t* positions, int64_t R, int64_t block, int64_t bpb, int64_t rows,
+                                      int32_t* counts) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < R) {
+        int64_t v = (int64_t)positions[i] / block * bpb;
+        counts[i] = (int32_t)(v < rows ? v : rows);
+    }
+}
+
+__global__ void pack_keys_kernel(const float* __restrict__ s, int64_t R, int64_t N, int64_t lds,
+                                 const int32_t* __restrict__ lengths, int64_t* __restrict__ keys, int64_t ldk) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= R * N) return;
+    int64_t r = i / N, n = i % N;
+    keys[r * ldk + n] = n < lengths[r] ? pack_key(s[r * lds + n], (int32_t)n) : kEmpty;
+}
+
+__global__ void unpack_kernel(const int64_t* __restrict__ keys, int64_t n, int32_t* __restrict__ ids) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) ids[i] = key_bucket(keys[i]);
+}
+
+// ------------------------------------------------------------------ top-k
+
+// Loader interface: key(n) for n < N. Sorted top-k of N keys into out[0..k) (EMPTY past N).
+// Shared: kSortCap int64. When N fits the buffer: one bitonic sort. Otherwise the running
+// best k2 = next_pow2(k) keys are kept at the front and merged with successive chunks.
+template <typename Loader>
+__device__ void block_topk(const Loader& key, int N, int k, int64_t* sbuf, int64_t* out, int ldo_k) {
+    int n2 = next_pow2(max(N, 1));
+    if (n2 <= kSortCap) {
+        for (int i = threadIdx.x; i < n2; i += blockDim.x) sbuf[i] = i < N ? key(i) : kEmpty;
+        __syncthreads();
+        bitonic_sort_desc(sbuf, n2);
+        for (int i = threadIdx.x; i < ldo_k; i += blockDim.x) out[i] = i < k ? sbuf[i] : kEmpty;
+        __syncthreads();
+        return;
+    }
+    int k2 = next_pow2(k);
+    int chunk = kSortCap - k2;
+    for (int i = threadIdx.x; i < k2; i += blockDim.x) sbuf[i] = kEmpty;
+    for (int start = 0; start < N; start += chunk) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < chunk; i += blockDim.x) sbuf[k2 + i] = start + i < N ? key(start + i) : kEmpty;
+        __syncthreads();
+        bitonic_sort_desc(sbuf, kSortCap);
+    }
+    for (int i = threadIdx.x; i < ldo_k; i += blockDim.x) out[i] = i < k ? sbuf[i] : kEmpty;
+    __syncthreads();
+}
+
+struct MaskedKeys {
+    const int64_t* row;
+    int count;  // slots at or past count read as EMPTY (upstream TopK.best()'s ~listed mask)
+    __device__ int64_t operator()(int i) const { return i < count ? row[i] : kEmpty; }
+};
+
+struct PackedScores {
+    const float* row;
+    int live;
+    __device__ int64_t operator()(int i) const { return i < live ? pack_key(row[i], i) : kEmpty; }
+};
+
+// best_first_keys (pipeline.py:189-214): masked, sorted descending, k = min(top_p, N).
+__global__ void __launch_bounds__(1024) best_first_kernel(const int64_t* __restrict__ keys, int64_t N, int64_t ldk,
+                                                          int k, const int32_t* __restrict__ counts,
+                                                          int64_t* __restrict__ out, int64_t ldo) {
+    extern __shared__ int64_t sbuf[];
+    int r = blockIdx.x;
+    int cnt = counts ? min((int64_t)counts[r], N) : (int)N;
+    cnt = max(cnt, 0);
+    MaskedKeys loader{keys + r * ldk, cnt};
+    block_topk(loader, (int)N, k, sbuf, out + r * ldo, (int)ldo);
+}
+
+// select_topk_scores (select_fused.py:52-80): scores -> K2 greatest packed keys.
+__global__ void __launch_bounds__(1024) select_topk_kernel(const float* __restrict__ s, int64_t N, int64_t lds,
+                                                           const int32_t* __restrict__ lengths, int k,
+                                                           int64_t* __restrict__ out, int64_t ldo) {
+    extern __shared__ int64_t sbuf[];
+    int r = blockIdx.x;
+    int live = (int)min((int64_t)max(lengths[r], 0), N);
+    PackedScores loader{s + r * lds, live};
+    block_topk(loader, (int)N, k, sbuf, out + r * ldo, (int)ldo);
+}
+
+// ------------------------------------------------------------------ expansion
+
+struct PickFromIds {
+    const int32_t* row;
+    __device__ int32_t operator()(int p) const { return row[p]; }
+};
+struct PickFromKeys {
+    const int64_t* row;
+    __device__ int32_t operator()(int p) const { return key_bucket(row[p]); }
+};
+
+// The rank-order walk of one row (select_fused.py:172-214) by the whole block:
+// slots (pick, member) in walk order; keep ids with sink <= id < window_start; the first
+// top_k kept, then the window [window_start, pos] and the sinks [0, min(sink, ws)).
+template <typename Picks>
+__device__ void expand_row(const Picks& pick_of, int P, const int32_t* __restrict__ members, int64_t member_rows,
+                           int cap, int64_t pos, int window, int sink, int top_k, int32_t* __restrict__ out,
+                           int width, int32_t* length_out, int* scan_smem) {
+    int64_t ws = pos + 1 - window;
+    if (ws < 0) ws = 0;
+    constexpr int SPT = 4;
+    int tile = blockDim.x * SPT;
+    int total_slots = P * cap;
+    int filled = 0;
+    for (int t0 = 0; t0 < total_slots && filled < top_k; t0 += tile) {
+        int ids[SPT];
+        int cnt = 0;
+#pragma unroll
+        for (int e = 0; e < SPT; ++e) {
+            int s = t0 + threadIdx.x * SPT + e;
+            int id = -1;
+            if (s < total_slots) {
+                int p = s / cap, m = s - p * cap;
+                int b = pick_of(p);
+                if (b >= 0 && b < member_rows) {
+                    int v = members[(int64_t)b * cap + m];
+                    if (v >= sink && v < ws) id = v;
+                }
+            }
+            ids[e] = id;
+            cnt += id >= 0;
+        }
+        int total;
+        int at = filled + block_exclusive_scan(cnt, scan_smem, &total);
+#pragma unroll
+        for (int e = 0; e < SPT; ++e) {
+            if (ids[e] >= 0) {
+                if (at < top_k) out[at] = ids[e];
+                ++at;
+            }
+        }
+        filled += total;
+    }
+    if (filled > top_k) filled = top_k;
+    int nwin = (int)(pos - ws + 1);
+    if (nwin < 0) nwin = 0;
+    int nsink = (int)(sink < ws ? sink : ws);
+    int length = filled + nwin + nsink;
+    for (int i = threadIdx.x; i < width - filled; i += blockDim.x) {
+        int j = filled + i, v = -1;
+        if (i < nwin) v = (int)(ws + i);
+        else if (i < nwin + nsink) v = i - nwin;
+        out[j] = v;
+    }
+    if (threadIdx.x == 0) *length_out = length;
+}
+
+template <typename PickT>
+__global__ void __launch_bounds__(512) expand_kernel(const PickT* __restrict__ picks, int P, int64_t ldp,
+                                                     const int32_t* __restrict__ members, int64_t member_rows, int cap,
+                                                     const int32_t* __restrict__ positions, int window, int sink,
+                                                     int top_k, int32_t* __restrict__ lists,
+                                                     int32_t* __restrict__ lengths) {
+    __shared__ int scan_smem[33];
+    int r = blockIdx.x;
+    int width = top_k + window + sink;
+    if constexpr (sizeof(PickT) == 8) {
+        PickFromKeys pk{reinterpret_cast<const int64_t*>(picks) + r * ldp};
+        expand_row(pk, P, members, member_rows, cap, positions[r], window, sink, top_k, lists + (int64_t)r * width,
+                   width, lengths + r, scan_smem);
+    } else {
+        PickFromIds pk{reinterpret_cast<const int32_t*>(picks) + r * ldp};
+        expand_row(pk, P, members, member_rows, cap, positions[r], window, sink, top_k, lists + (int64_t)r * width,
+                   width, lengths + r, scan_smem);
+    }
+}
+
+// ------------------------------------------------------------------ fused select
+
+struct SmemPicks {
+    const int64_t* keys;
+    __device__ int32_t operator()(int p) const { return key_bucket(keys[p]); }
+};
+
+struct GlobalKeysCg {
+    const int64_t* row;
+    int count;
+    __device__ int64_t operator()(int i) const { return i < count ? __ldcg(row + i) : kEmpty; }
+};
+
+// One launch from index queries to read lists. grid = (chunks, R), block = 256.
+// Workspace: keys [R, N] int64 and tickets [R] int32 (zero at allocation; the last CTA of a
+// row resets its ticket, so the launch can be replayed, e.g. from a CUDA graph).
+template <typename TQ, typename TC, int CHUNKS>
+__global__ void __launch_bounds__(256) select_fused_kernel(
+    const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d,
+    const int32_t* __restrict__ positions, int64_t block, int64_t bpb, int cols_per_cta, int top_p,
+    const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
+    int32_t* __restrict__ lengths, int64_t* __restrict__ ws_keys, int32_t* __restrict__ tickets) {
+    extern __shared__ int64_t sbuf[];
+    __shared__ int scan_smem[33];
+    __shared__ int is_last;
+    int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int64_t pos = positions[r];
+    int64_t vis = pos / block * bpb;
+    int count = (int)(vis < N ? vis : N);
+    if (count < 0) count = 0;
+    int64_t c0 = (int64_t)blockIdx.x * cols_per_cta;
+    int64_t c1 = min(c0 + cols_per_cta, (int64_t)count);
+    if (c0 < c1) {
+        int nchunks = d >> 3;
+        float x[CHUNKS][8];
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j) {
+            int ch = lane + 32 * j;
+            if (ch < nchunks) load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+        }
+        for (int64_t n = c0 + warp; n < c1; n += blockDim.x >> 5) {
+            float p = butterfly_sum(lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks));
+            if (lane == 0) ws_keys[r * N + n] = pack_key(p, (int32_t)n);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = atomicAdd(tickets + r, 1);
+        is_last = (t == (int)gridDim.x - 1);
+        if (is_last) tickets[r] = 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    int k = (int)min((int64_t)top_p, N);
+    GlobalKeysCg loader{ws_keys + r * N, count};
+    int n2 = next_pow2(max(count, 1));
+    int64_t* picks = sbuf;  // sorted keys live at the front of the buffer
+    if (n2 <= kSortCap) {
+        // every live key sits below n2; picks in [n2, k) stay EMPTY
+        int fill = n2 > k ? n2 : k;
+        for (int i = threadIdx.x; i < fill; i += blockDim.x) sbuf[i] = loader(i);
+        __syncthreads();
+        bitonic_sort_desc(sbuf, n2);
+    } else {
+        block_topk(loader, count, k, sbuf, sbuf, k);  // in-place: out aliases the buffer front
+    }
+    int width = top_k + window + sink;
+    SmemPicks pk{picks};
+    expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+               scan_smem);
+}
+
+// ------------------------------------------------------------------ host helpers
+
+template <typename K>
+static int set_smem(K kernel, int bytes) {
+    if (bytes > 48 * 1024) {
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+            return LSA_ERR_CUDA;
+    }
+    return LSA_OK;
+}
+
+static int sort_smem_bytes(int64_t N) {
+    int n2 = next_pow2((int)(N > 0 ? N : 1));
+    return (n2 <= kSortCap ? n2 : kSortCap) * 8;
+}
+
+template <typename TQ, typename TC>
+static int launch_scores(const void* q, int64_t R, int64_t ldq, const void* c, int64_t N, int64_t d, float* out,
+                         int64_t ldo, cudaStream_t st) {
+    int chunks = (int)((d / 8 + 31) / 32);
+    int cols = 64;
+    dim3 grid((unsigned)((N + cols - 1) / cols), (unsigned)R);
+    if (grid.x == 0 || R == 0) return LSA_OK;
+    auto qq = (const TQ*)q;
+    auto cc = (const TC*)c;
+#define LSA_SC(CH) scores_kernel<TQ, TC, CH><<<grid, 256, 0, st>>>(qq, ldq, cc, N, (int)d, out, ldo, cols)
+    if (chunks <= 1) LSA_SC(1);
+    else if (chunks <= 2) LSA_SC(2);
+    else if (chunks <= 4) LSA_SC(4);
+    else if (chunks <= 8) LSA_SC(8);
+    else return LSA_ERR_ARG;
+#undef LSA_SC
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+}  // namespace lsa
+
+using namespace lsa;
+
+static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+extern "C" {
+
+int lsa_bucket_scores(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                      int64_t N, int64_t d, float* scores, int64_t lds, cudaStream_t stream) {
+    if (d <= 0 || d % 8 || d > 2048 || R < 0 || N < 0 || ldq % 8) return LSA_ERR_ARG;
+    if (!aligned16(queries) || !aligned16(centroids)) return LSA_ERR_ARG;
+    if (q_dtype == kBF16 && c_dtype == kBF16)
+        return launch_scores<__nv_bfloat16, __nv_bfloat16>(queries, R, ldq, centroids, N, d, scores, lds, stream);
+    if (q_dtype == kF32 && c_dtype == kF32)
+        return launch_scores<float, float>(queries, R, ldq, centroids, N, d, scores, lds, stream);
+    if (q_dtype == kF32 && c_dtype == kBF16)
+        return launch_scores<float, __nv_bfloat16>(queries, R, ldq, centroids, N, d, scores, lds, stream);
+    return LSA_ERR_ARG;
+}
+
+int lsa_visible_counts(const int32_t* positions, int64_t R, int64_t block, int64_t bpb, int64_t rows, int32_t* counts,
+                       cudaStream_t stream) {
+    if (block <= 0 || bpb < 0) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    visible_counts_kernel<<<(unsigned)((R + 255) / 256), 256, 0, stream>>>(positions, R, block, bpb, rows, counts);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_pack_keys(const float* scores, int64_t R, int64_t N, int64_t lds, const int32_t* lengths, int64_t* keys,
+                  int64_t ldk, cudaStream_t stream) {
+    if (R * N == 0) return LSA_OK;
+    pack_keys_kernel<<<(unsigned)((R * N + 255) / 256), 256, 0, stream>>>(scores, R, N, lds, lengths, keys, ldk);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_best_first_keys(const int64_t* keys, int64_t R, int64_t N, int64_t ldk, int64_t k, const int32_t* counts,
+                        int64_t* out, int64_t ldo, cudaStream_t stream) {
+    if (k < 0 || k > 4096 || ldo < k) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    int smem = sort_smem_bytes(N);
+    if (set_smem(best_first_kernel, smem)) return LSA_ERR_CUDA;
+    best_first_kernel<<<(unsigned)R, 1024, smem, stream>>>(keys, N, ldk, (int)k, counts, out, ldo);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_unpack_ids(const int64_t* keys, int64_t n, int32_t* ids, cudaStream_t stream) {
+    if (n == 0) return LSA_OK;
+    unpack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(keys, n, ids);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_select_topk_scores(const float* scores, int64_t R, int64_t N, int64_t lds, const int32_t* lengths,
+                           int64_t top_p, int64_t* out, int64_t ldo, cudaStream_t stream) {
+    int64_t k = top_p < N ? top_p : N;
+    if (k < 0 || k > 4096 || ldo < k) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    int smem = sort_smem_bytes(N);
+    if (set_smem(select_topk_kernel, smem)) return LSA_ERR_CUDA;
+    select_topk_kernel<<<(unsigned)R, 1024, smem, stream>>>(scores, N, lds, lengths, (int)k, out, ldo);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_expand_in_order(const int32_t* picked, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
+                        int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                        int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
+    if (cap <= 0 || window < 0 || sink < 0 || top_k < 0 || P < 0) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    expand_kernel<int32_t><<<(unsigned)R, 512, 0, stream>>>(picked, (int)P, ldp, members, member_rows, (int)cap,
+                                                           positions, (int)window, (int)sink, (int)top_k, lists,
+                                                           lengths);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk, const int32_t* members,
+                         int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                         int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
+    if (cap <= 0 || window < 0 || sink < 0 || top_k < 0 || P < 0) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    expand_kernel<int64_t><<<(unsigned)R, 512, 0, stream>>>(keys, (int)P, ldk, members, member_rows, (int)cap,
+                                                           positions, (int)window, (int)sink, (int)top_k, lists,
+                                                           lengths);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+// Scratch of lsa_select_fused: the packed keys [R, N] int64. Counters: one int32 ticket
+// per row, zero before the call; the kernel leaves them zero.
+int64_t lsa_select_fused_scratch(int64_t R, int64_t N) { return ((R * N * 8 + 255) / 256) * 256; }
+
+int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                     int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
+                     int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
+                     int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                     int64_t max_position, cudaStream_t stream) {
+    if (d <= 0 || d % 8 || d > 2048 || ldq % 8 || cap <= 0 || block <= 0) return LSA_ERR_ARG;
+    if (!aligned16(queries) || !aligned16(centroids) || !aligned16(scratch)) return LSA_ERR_ARG;
+    if (top_p > 4096 || scratch_bytes < lsa_select_fused_scratch(R, N) || n_counters < R) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    int64_t* ws_keys = (int64_t*)scratch;
+    int32_t* tickets = counters;
+    // columns any row can see: the grid covers the widest row (max_position < 0: all N)
+    int64_t most = max_position < 0 ? N : (max_position / block * bpb < N ? max_position / block * bpb : N);
+    int cols = 8;  // one column per warp: the centroid read spreads over many SMs
+    int chunks_x = (int)((most + cols - 1) / cols);
+    if (chunks_x < 1) chunks_x = 1;
+    dim3 grid((unsigned)chunks_x, (unsigned)R);
+    int smem = sort_smem_bytes(most);
+    if (smem < top_p * 8) smem = (int)(top_p * 8);
+    int ch = (int)((d / 8 + 31) / 32);
+#define LSA_FS(TQ, TC, CH)                                                                                            \
+    do {                                                                                                              \
+        auto kern = select_fused_kernel<TQ, TC, CH>;                                                                  \
+        if (set_smem(kern, smem)) return LSA_ERR_CUDA;                                                                \
+        kern<<<grid, 256, smem, stream>>>((const TQ*)queries, ldq, (const TC*)centroids, N, (int)d, positions, block, \
+                                          bpb, cols, (int)top_p, members, (int)cap, (int)window, (int)sink,           \
+                                          (int)top_k, lists, lengths, ws_keys, tickets);                             \
+    } while (0)
+#define LSA_FS_CH(TQ, TC)              \
+    do {                               \
+        if (ch <= 1) LSA_FS(TQ, TC, 1);  \
+        else if (ch <= 2) LSA_FS(TQ, TC, 2); \
+        else if (ch <= 4) LSA_FS(TQ, TC, 4); \
+        else LSA_FS(TQ, TC, 8);          \
+    } while (0)
+    if (q_dtype == kBF16 && c_dtype == kBF16) LSA_FS_CH(__nv_bfloat16, __nv_bfloat16);
+    else if (q_dtype == kF32 && c_dtype == kF32) LSA_FS_CH(float, float);
+    else if (q_dtype == kF32 && c_dtype == kBF16) LSA_FS_CH(float, __nv_bfloat16);
+    else return LSA_ERR_ARG;
+#undef LSA_FS_CH
+#undef LSA_FS
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+}  // extern "C"

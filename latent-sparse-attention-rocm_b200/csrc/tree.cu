@@ -1,0 +1,260 @@
+// tree.cu - the D-LSA tree beam: levels walked top-down, candidates scored by centroid,
+// the best beam_width kept per level, top_p buckets picked at level 0 (sm_100a).
+//
+// Reference (AIwork4me/latent-sparse-attention-rocm, paths inside that project):
+//   beam             src/lsa_rocm_lab/port/_tree.py:318-373 (_beam_pick_rows)
+//   growth replay    _tree.py:100-142 (_growth_replay; upstream growth_at)
+// Growth in closed form (equal to the replay's loop for every page p; checked on CPU):
+//   covered = floor(p * bpb / nb) * nb; made[0] = covered / size;
+//   closed[l] = floor(made[l] / nb) * nb, made[l + 1] = closed[l] / size (l < top_level - 1);
+//   closed[top_level - 1] = 0; levels = number of levels with made > 0.
+// Candidates at level L are the carried children plus [first_open, made[L-1]) (first_open
+// = 0 on the row's top level, else closed[L-1]); carried and fresh ranges are disjoint, so
+// no dedup is needed. Order: packed key ordered_bits(cdot(q, centroid)) | (0x7FFFFFFF - id),
+// descending - score first, the lower id on ties. Scores: canonical fp32 cdot.
+//
+// Launches: one per node level (top down) and one for level 0. Each launch scores its
+// candidates over a grid of CTAs; the last CTA of a row (atomic ticket) sorts the row's
+// keys and writes the next level's carried rows (or the picks).
+#include "common.cuh"
+
+namespace lsa {
+
+constexpr int kTreeMaxLevels = 8;
+constexpr int kTreeSortCap = 8192;
+
+struct TreeGrowth {
+    int32_t covered, levels;
+    int32_t made[kTreeMaxLevels], closed[kTreeMaxLevels];
+};
+
+__device__ __forceinline__ void growth_at(int64_t page, int64_t bpb, int64_t nb, int64_t size, int top_level,
+                                          int64_t rows, int n_built, TreeGrowth& g) {
+    int64_t end = page * bpb;
+    if (end > rows) end = rows;  // a position past the cache sees the cache's buckets
+    int64_t covered = end / nb * nb;
+    int64_t made = covered / size;
+    g.covered = (int32_t)covered;
+    g.levels = 0;
+    for (int l = 0; l < kTreeMaxLevels; ++l) g.made[l] = g.closed[l] = 0;
+    for (int l = 0; l < top_level && l < kTreeMaxLevels; ++l) {
+        g.made[l] = (int32_t)made;
+        if (made > 0) g.levels = l + 1;
+        if (l + 1 < top_level) {
+            int64_t closed = made / nb * nb;
+            g.closed[l] = (int32_t)closed;
+            made = closed / size;
+        }
+    }
+    if (g.levels > n_built) g.levels = n_built;
+}
+
+struct TreeLevelArgs {
+    const float* q;  // [R, d] fp32 index queries
+    int64_t d;
+    const int32_t* positions;
+    int64_t block, bpb, nb, size, rows;
+    int top_level, n_built;
+    int L;                       // node level of this launch (0 = buckets)
+    const float* centroids;      // level L centroids (L >= 1) or bucket centroids_f32 (L == 0)
+    const int64_t* children;     // level L children [n, size] (L >= 1)
+    int keep;                    // beam_width (L >= 1) or top_p (L == 0)
+    const int32_t* carried_in;   // [R, carry_cap]
+    const int32_t* carried_n_in; // [R]
+    int32_t* carried_out;        // [R, carry_cap]
+    int32_t* carried_n_out;      // [R]
+    int carry_cap;
+    int32_t* picks;              // [R, top_p] (L == 0)
+    int64_t* ws_keys;            // [R, cand_cap]
+    int cand_cap;
+    int32_t* tickets;            // [R]
+    int32_t* status;
+};
+
+template <int CHUNKS>
+__global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
+    extern __shared__ int64_t tsm[];
+    __shared__ int is_last;
+    const int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int64_t pos = a.positions[r];
+    int64_t page = pos / a.block;
+    TreeGrowth g;
+    growth_at(page, a.bpb, a.nb, a.size, a.top_level, a.rows, a.n_built, g);
+    const bool active = a.L == 0 || g.levels >= a.L;
+    int n_carried = 0, fresh0 = 0, fresh1 = 0;
+    if (active) {
+        if (a.L == 0) {
+            n_carried = g.levels > 0 ? a.carried_n_in[r] : 0;
+            int64_t vis = page * a.bpb;
+            fresh0 = g.levels > 0 ? g.covered : 0;
+            fresh1 = (int)(vis < a.rows ? vis : a.rows);
+        } else {
+            n_carried = g.levels > a.L ? a.carried_n_in[r] : 0;
+            fresh0 = g.levels == a.L ? 0 : g.closed[a.L - 1];
+            fresh1 = g.made[a.L - 1];
+        }
+        if (fresh1 < fresh0) fresh1 = fresh0;
+    }
+    int n_cand = n_carried + (fresh1 - fresh0);
+    if (n_cand > a.cand_cap) {  // never for a consistent hierarchy; recorded, then clamped
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(a.status, LSA_ERR_ARG);
+        n_cand = a.cand_cap;
+    }
+    // phase 1: score this CTA's share of the row's candidates
+    if (active && n_cand > 0) {
+        int nchunks = (int)(a.d >> 3);
+        float x[CHUNKS][8];
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j) {
+            int ch = lane + 32 * j;
+            if (ch < nchunks) load8<float>(a.q + r * a.d + (size_t)ch * 8, x[j]);
+        }
+        for (int i = blockIdx.x * nw + warp; i < n_cand; i += gridDim.x * nw) {
+            int id = i < n_carried ? a.carried_in[(int64_t)r * a.carry_cap + i] : fresh0 + (i - n_carried);
+            float s = butterfly_sum(lane_partial_regs<float, CHUNKS>(x, a.centroids + (int64_t)id * a.d, lane,
+                                                                     nchunks));
+            if (lane == 0) a.ws_keys[(int64_t)r * a.cand_cap + i] = pack_key(s, id);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = atomicAdd(a.tickets + r, 1);
+        is_last = t == (int)gridDim.x - 1;
+        if (is_last) a.tickets[r] = 0;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // phase 2 (last CTA of the row): order the candidates, keep the best
+    int kept = 0;
+    if (active && n_cand > 0) {
+        int n2 = next_pow2(n_cand);
+        for (int i = threadIdx.x; i < n2; i += blockDim.x)
+            tsm[i] = i < n_cand ? __ldcg(a.ws_keys + (int64_t)r * a.cand_cap + i) : kEmpty;
+        __syncthreads();
+        bitonic_sort_desc(tsm, n2);
+        kept = n_cand < a.keep ? n_cand : a.keep;
+    }
+    if (a.L == 0) {
+        for (int i = threadIdx.x; i < a.keep; i += blockDim.x)
+            a.picks[(int64_t)r * a.keep + i] = i < kept ? key_bucket(tsm[i]) : -1;
+    } else {
+        int S = (int)a.size;
+        for (int i = threadIdx.x; i < kept * S; i += blockDim.x) {
+            int node = key_bucket(tsm[i / S]);
+            a.carried_out[(int64_t)r * a.carry_cap + i] = (int32_t)a.children[(int64_t)node * S + (i % S)];
+        }
+        if (threadIdx.x == 0) a.carried_n_out[r] = active ? kept * S : 0;
+    }
+}
+
+static int64_t r256(int64_t x) { return (x + 255) / 256 * 256; }
+
+struct TreePlan {
+    int carry_cap, cand_cap;
+    int64_t keys_bytes, carry_bytes, scratch_bytes, counters;
+};
+
+static TreePlan plan_tree(int64_t R, int64_t n_built, const int64_t* level_counts, int64_t beam, int64_t size,
+                          int64_t nb, int64_t bpb, int64_t top_p) {
+    TreePlan p;
+    int64_t carry = beam * size;
+    int64_t thr = bpb / nb > 1 ? bpb / nb : 1;
+    int64_t cand = carry + nb * thr + 1;  // level 0 bound
+    for (int64_t l = 0; l < n_built; ++l) {
+        int64_t c = level_counts[l] > carry + nb ? level_counts[l] : carry + nb;
+        if (c > cand) cand = c;
+    }
+    (void)top_p;
+    p.carry_cap = (int)(carry > 0 ? carry : 1);
+    p.cand_cap = (int)cand;
+    p.keys_bytes = r256(R * cand * 8);
+    p.carry_bytes = r256(R * p.carry_cap * 4) * 2 + r256(R * 4) * 2;
+    p.scratch_bytes = p.keys_bytes + p.carry_bytes;
+    p.counters = R + 1;
+    return p;
+}
+
+}  // namespace lsa
+
+using namespace lsa;
+
+extern "C" {
+
+int lsa_tree_plan(int64_t R, int64_t n_built, const int64_t* level_counts, int64_t beam, int64_t size, int64_t nb,
+                  int64_t bpb, int64_t top_p, int64_t* scratch_bytes, int64_t* n_counters) {
+    if (n_built < 0 || n_built > kTreeMaxLevels || beam <= 0 || size <= 0 || nb <= 0) return LSA_ERR_ARG;
+    TreePlan p = plan_tree(R, n_built, level_counts, beam, size, nb, bpb, top_p);
+    if (p.cand_cap > kTreeSortCap) return LSA_ERR_ARG;
+    if (scratch_bytes) *scratch_bytes = p.scratch_bytes;
+    if (n_counters) *n_counters = p.counters;
+    return LSA_OK;
+}
+
+// Tree beam picks [R, top_p] int32 (-1 padded). level_centroids / level_children /
+// level_counts are HOST arrays of n_built entries (device pointers / node counts).
+int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                    int64_t rows, int64_t n_built, const float* const* level_centroids,
+                    const int64_t* const* level_children, const int64_t* level_counts, const float* bucket_centroids,
+                    int64_t size, int64_t nb, int64_t top_level, int64_t beam, int64_t top_p, int32_t* picks,
+                    void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream) {
+    if (d <= 0 || d % 8 || d > 2048 || ((uintptr_t)q & 15) || top_level > kTreeMaxLevels || n_built > top_level)
+        return LSA_ERR_ARG;
+    if (top_p <= 0 || top_p > kTreeSortCap || block <= 0) return LSA_ERR_ARG;
+    TreePlan p = plan_tree(R, n_built, level_counts, beam, size, nb, bpb, top_p);
+    if (p.cand_cap > kTreeSortCap || scratch_bytes < p.scratch_bytes || n_counters < p.counters) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    char* w = (char*)scratch;
+    TreeLevelArgs a;
+    a.q = q; a.d = d; a.positions = positions; a.block = block; a.bpb = bpb; a.nb = nb; a.size = size;
+    a.rows = rows; a.top_level = (int)top_level; a.n_built = (int)n_built;
+    a.ws_keys = (int64_t*)w;
+    a.cand_cap = p.cand_cap;
+    a.carry_cap = p.carry_cap;
+    int32_t* carry[2] = {(int32_t*)(w + p.keys_bytes), (int32_t*)(w + p.keys_bytes + r256(R * p.carry_cap * 4))};
+    int32_t* carry_n[2] = {(int32_t*)(w + p.keys_bytes + 2 * r256(R * p.carry_cap * 4)),
+                           (int32_t*)(w + p.keys_bytes + 2 * r256(R * p.carry_cap * 4) + r256(R * 4))};
+    a.tickets = counters;
+    a.status = counters + R;
+    a.picks = picks;
+    int chunks = (int)((d / 8 + 31) / 32);
+    int smem = next_pow2(p.cand_cap) * 8;
+    if (smem < 1024) smem = 1024;
+    int cur = 0;
+    for (int64_t L = n_built; L >= 0; --L) {
+        a.L = (int)L;
+        a.centroids = L > 0 ? level_centroids[L - 1] : bucket_centroids;
+        a.children = L > 0 ? level_children[L - 1] : nullptr;
+        a.keep = (int)(L > 0 ? beam : top_p);
+        a.carried_in = carry[cur];
+        a.carried_n_in = carry_n[cur];
+        a.carried_out = carry[cur ^ 1];
+        a.carried_n_out = carry_n[cur ^ 1];
+        int64_t bound = L > 0 ? (level_counts[L - 1] > p.carry_cap + nb ? level_counts[L - 1] : p.carry_cap + nb)
+                              : p.cand_cap;
+        int64_t want = (bound + 63) / 64;  // 8 warps x 8 candidates per CTA
+        int64_t spread = (296 + R - 1) / R;  // about two CTAs per SM over all rows
+        unsigned gx = (unsigned)(want < spread ? want : spread);
+        if (gx < 1) gx = 1;
+        dim3 grid(gx, (unsigned)R);
+#define LSA_TL(CH)                                                                                         \
+    do {                                                                                                   \
+        auto kern = tree_level_kernel<CH>;                                                                 \
+        if (smem > 48 * 1024 &&                                                                            \
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) \
+            return LSA_ERR_CUDA;                                                                           \
+        kern<<<grid, 256, smem, stream>>>(a);                                                              \
+    } while (0)
+        if (chunks <= 1) LSA_TL(1);
+        else if (chunks <= 2) LSA_TL(2);
+        else if (chunks <= 4) LSA_TL(4);
+        else LSA_TL(8);
+#undef LSA_TL
+        LSA_LAUNCH_CHECK();
+        cur ^= 1;
+    }
+    return LSA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,142 @@
+"""ctypes binding of ``liblsa_b200.so`` - the C-ABI every operator of this package calls.
+
+There is no fallback: if the library is missing, or a tensor is not on a CUDA device,
+the operators raise. Streams: every call launches on torch's current stream of the
+tensors' device. Workspaces: scratch (any content) and counters (int32, zero at rest; the
+kernels that use them leave them zero) are cached per (device, stream) and only grow.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+import torch
+
+LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblsa_b200.so"
+
+F32, F16, BF16 = 0, 1, 2
+DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_SHORT = 0, -1, -2, -3, -4
+
+_lib = None
+_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int64
+_INT = ctypes.c_int
+_F = ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/lsa_b200.h
+SIGNATURES = {
+    "lsa_bucket_scores": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _I, _P, _I, _P]),
+    "lsa_visible_counts": (_INT, [_P, _I, _I, _I, _I, _P, _P]),
+    "lsa_pack_keys": (_INT, [_P, _I, _I, _I, _P, _P, _I, _P]),
+    "lsa_best_first_keys": (_INT, [_P, _I, _I, _I, _I, _P, _P, _I, _P]),
+    "lsa_unpack_ids": (_INT, [_P, _I, _P, _P]),
+    "lsa_select_topk_scores": (_INT, [_P, _I, _I, _I, _P, _I, _P, _I, _P]),
+    "lsa_expand_in_order": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "lsa_expand_from_keys": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "lsa_select_fused_scratch": (_I, [_I, _I]),
+    "lsa_select_fused": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P, _P,
+                                _I, _P, _I, _I, _P]),
+    "lsa_sparse_read_plan": (_INT, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "lsa_sparse_read": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _I, _I,
+                               _P]),
+    "lsa_regroup": (_INT, [_P, _P, _INT, _I, _I, _I, _I, _P, _P, _P]),
+    "lsa_normalize_rows": (_INT, [_P, _I, _I, _P, _P, _P]),
+    "lsa_build_buckets_workspace": (_I, [_I, _I, _I, _I]),
+    "lsa_build_buckets": (_INT, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P]),
+    "lsa_position_buckets": (_INT, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "lsa_pair_to_size_workspace": (_I, [_I, _I, _I]),
+    "lsa_pair_to_size": (_INT, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P]),
+    "lsa_tree_plan": (_INT, [_I, _I, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "lsa_tree_select": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P,
+                               _I, _P]),
+}
+
+
+def lib():
+    """The loaded library; raises when it has not been built (no CPU fallback exists)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: the LSA kernels are CUDA-only; build them with "
+                        "`python latent-sparse-attention-rocm_b200/build.py` (or __graft_entry__.build())"
+                    )
+                handle = ctypes.CDLL(str(LIB_PATH))
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                _lib = handle
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return sorted(SIGNATURES)
+
+
+def check(rc: int, what: str) -> None:
+    if rc == OK:
+        return
+    if rc == ERR_ARG:
+        raise ValueError(f"{what}: arguments rejected by the kernel entry point")
+    if rc == ERR_TIMEOUT:
+        raise RuntimeError(f"{what}: a bounded device wait expired")
+    if rc == ERR_SHORT:
+        raise ValueError(f"{what}: a cluster block could not reach its bucket count under the cap")
+    raise RuntimeError(f"{what}: CUDA launch failed (status {rc})")
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*tensors: torch.Tensor, what: str, exc=ValueError) -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise exc(f"{what} is a CUDA kernel (B200, sm_100a), got device {t.device}")
+
+
+class _Workspace:
+    def __init__(self):
+        self.scratch: dict = {}
+        self.counters: dict = {}
+
+
+_ws = _Workspace()
+
+
+def _key(device: torch.device):
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return (idx, torch.cuda.current_stream(device).cuda_stream)
+
+
+def scratch(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Cached scratch bytes (any content) for the current stream of ``device``."""
+    key = _key(device)
+    buf = _ws.scratch.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _ws.scratch[key] = buf
+    return buf
+
+
+def counters(n: int, device: torch.device) -> torch.Tensor:
+    """Cached int32 counters, zero at rest, for the current stream of ``device``."""
+    key = _key(device)
+    buf = _ws.counters.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.zeros(max(int(n), 64), dtype=torch.int32, device=device)
+        _ws.counters[key] = buf
+    return buf

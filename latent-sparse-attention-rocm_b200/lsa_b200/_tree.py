@@ -1,0 +1,81 @@
+"""The D-LSA tree select on B200 - drop-in for ``lsa_rocm_lab.port._tree``.
+
+Reference: AIwork4me/latent-sparse-attention-rocm, ``src/lsa_rocm_lab/port/_tree.py``
+(switch ``:34-60``, beam ``:318-373``, growth replay ``:100-142``).
+
+The beam runs as one ``lsa_tree_select`` call: a launch per node level, top down, and one
+for the buckets, each scoring its candidates over many CTAs and ordering them in the row's
+last CTA (packed keys: score first, the lower id on ties). The growth each query's page
+saw is computed in closed form on the device - no host sync, CUDA-graph safe. The picks
+go through the same expansion kernel as the flat select.
+
+``LSA_TREE_IMPL`` (``per_page`` default / ``batched``) names the reference's two torch
+walks; both map to this one kernel, which is set-equal to either by construction. This
+build emits only unique, valid picks (a short level pads with -1; the reference's batched
+walk does the same, ``_tree.py:279-282``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from . import _lib
+from ._lib import check, lib, ptr, require_cuda, stream_of
+
+
+def tree_picks(index_queries, positions, buckets, hierarchy, config) -> torch.Tensor:
+    """Best-first bucket picks [R, top_p] int32 (-1 padded) of the beam."""
+    require_cuda(index_queries, positions, what="tree_select")
+    if positions.shape[0] != index_queries.shape[0]:
+        raise ValueError(f"a position a query: {index_queries.shape[0]} queries, {positions.shape[0]} positions")
+    if config.start_nodes is not None:
+        raise ValueError("the beam covers start_nodes=None (the top level down), as the reference's exact walk")
+    if buckets.centroids_f32 is None:
+        raise ValueError("tree_select scores buckets with centroids_f32")
+    q = index_queries.float().contiguous()
+    pos = positions.to(torch.int32).contiguous()
+    R, d = q.shape
+    dev = q.device
+    levels = hierarchy.levels
+    n = len(levels)
+    picks = torch.empty(R, config.top_p, dtype=torch.int32, device=dev)
+    if R == 0:
+        return picks
+    counts = (ctypes.c_int64 * max(n, 1))(*[lv.centroids.shape[0] for lv in levels])
+    cents = [lv.centroids.float().contiguous() for lv in levels]
+    kids = [lv.children.to(torch.int64).contiguous() for lv in levels]
+    cptrs = (ctypes.c_void_p * max(n, 1))(*[c.data_ptr() for c in cents])
+    kptrs = (ctypes.c_void_p * max(n, 1))(*[c.data_ptr() for c in kids])
+    L = lib()
+    sb, nc = ctypes.c_int64(), ctypes.c_int64()
+    check(L.lsa_tree_plan(R, n, counts, config.beam_width, config.node_bucket_size, config.node_cluster_block_size,
+                          config.block_bucket_count, config.top_p, ctypes.byref(sb), ctypes.byref(nc)), "tree_select")
+    sc = _lib.scratch(sb.value, dev)
+    ct = _lib.counters(nc.value, dev)
+    bc = buckets.centroids_f32.float().contiguous()
+    check(L.lsa_tree_select(ptr(q), R, d, ptr(pos), config.cluster_block_size, config.block_bucket_count,
+                            buckets.rows, n, cptrs, kptrs, counts, ptr(bc), config.node_bucket_size,
+                            config.node_cluster_block_size, config.top_level, config.beam_width, config.top_p,
+                            ptr(picks), ptr(sc), sc.numel(), ptr(ct), ct.numel(), stream_of(q)), "tree_select")
+    return picks
+
+
+def tree_select_batched(index_queries, positions, buckets, hierarchy, config, top_k=None):
+    """Select by the beam, expand by the expansion kernel (ref ``_tree.py:34-60``)."""
+    os.environ.get("LSA_TREE_IMPL", "per_page")  # both walks are this one kernel
+    top_k = config.top_k if top_k is None else top_k
+    from .pipeline import expand_in_order
+
+    picks = tree_picks(index_queries, positions, buckets, hierarchy, config)
+    return expand_in_order(picks, buckets.members, positions, config.window_size, config.sink_size, top_k)
+
+
+def tree_select_per_page(index_queries, positions, buckets, hierarchy, config, top_k=None):
+    """The reference's per-page walk entry (ref ``_tree.py:63-85``) - the same kernel."""
+    return tree_select_batched(index_queries, positions, buckets, hierarchy, config, top_k)
+
+
+__all__ = ["tree_picks", "tree_select_batched", "tree_select_per_page", "_lib"]

@@ -1,0 +1,95 @@
+"""The C-ABI library loads and exports every symbol include/lsa_b200.h declares (CPU only).
+
+No compute call is made here (there may be no GPU); the Python binding's signature table
+must also cover exactly the header's entry points, and the header must compile as C.
+"""
+
+import pathlib
+import re
+import subprocess
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "lsa_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^(?:int|int64_t)\s+(lsa_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "lsa_sparse_read" in names and "lsa_select_fused" in names and "lsa_build_buckets" in names
+    assert len(names) >= 20
+
+
+def test_library_exports_every_declared_symbol():
+    from lsa_b200 import _lib
+
+    try:
+        L = _lib.lib()
+    except OSError as e:  # a machine without the CUDA runtime cannot dlopen it
+        pytest.skip(f"CUDA runtime not loadable here: {e}")
+    for name in _declared():
+        assert hasattr(L, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    exported = set(re.findall(r"\bT (lsa_\w+)", out.stdout))
+    assert set(_declared()) <= exported
+
+
+def test_binding_table_matches_header():
+    from lsa_b200 import _lib
+
+    assert sorted(_lib.SIGNATURES) == _declared()
+
+
+def test_header_compiles_as_c(tmp_path):
+    src = tmp_path / "use.c"
+    src.write_text('#include "lsa_b200.h"\nint main(void) { return lsa_sparse_read == 0; }\n')
+    res = subprocess.run(["gcc", "-fsyntax-only", "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include",
+                          str(src)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+
+
+def test_cpu_tensors_fail_loudly():
+    import torch
+
+    import lsa_b200
+
+    with pytest.raises(ValueError):
+        lsa_b200.select_fused.select_topk_scores(torch.zeros(2, 4), torch.zeros(2, dtype=torch.int32), 2)
+    with pytest.raises(AssertionError):
+        lsa_b200.read_kernel_tiled.sparse_read_auto(torch.zeros(1, 1, 2, 64), torch.zeros(1, 4, 2, 64),
+                                                    torch.zeros(1, 4, 2, 64), torch.zeros(1, 1, 4, dtype=torch.int32),
+                                                    torch.zeros(1, 1, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        lsa_b200.build_buckets_gpu(torch.zeros(64, 8), lsa_b200.PortConfig())
+
+
+def test_switch_validation_on_cpu(monkeypatch):
+    import torch
+
+    import lsa_b200
+
+    monkeypatch.setenv("LSA_SELECT_IMPL", "bogus")
+    with pytest.raises(ValueError, match="LSA_SELECT_IMPL"):
+        lsa_b200.flat_select(torch.zeros(2, 8), torch.tensor([7, 7]), None, lsa_b200.PortConfig())
+
+
+def test_dense_baseline_semantics_on_cpu():
+    """tests/test_dense_read.py:46-104 - decode row == prefill's last row; chunks bottom-right."""
+    import torch
+
+    import lsa_b200
+
+    torch.manual_seed(20261106)
+    q = torch.randn(1, 64, 8, 64) * 0.2
+    k = torch.randn(1, 64, 2, 64) * 0.2
+    v = torch.randn(1, 64, 2, 64) * 0.2
+    pre = lsa_b200.dense_read(q, k, v, 0.125)
+    assert torch.allclose(lsa_b200.dense_read(q[:, -1:], k, v, 0.125), pre[:, -1:], atol=1e-5)
+    assert torch.allclose(lsa_b200.dense_read(q[:, -7:], k, v, 0.125), pre[:, -7:], atol=1e-5)
+    with pytest.raises(ValueError):
+        lsa_b200.dense_read(q, k[:, :32], v[:, :32], 0.125)
