@@ -32,6 +32,7 @@ extern "C" {
 #define LSA_ERR_CUDA (-2)
 #define LSA_ERR_TIMEOUT (-3)
 #define LSA_ERR_SHORT (-4)
+#define LSA_ERR_SIZE (-5)
 
 /* ---------------------------------------------------------------- index space */
 
@@ -149,6 +150,18 @@ int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, cons
                     const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D,
                     int64_t width, float scale, void* out, void* scratch, int64_t scratch_bytes, int32_t* counters,
                     int64_t n_counters, int64_t splits, cudaStream_t stream);
+
+/* No counterpart in the reference: lsa_sparse_read for callers that cannot allocate
+ * device memory (a server whose device memory is one arena owned by its own allocator,
+ * a plugin host that forbids cudaMalloc once serving). The split partials and counters
+ * live in fixed __device__ arrays of this library: at most 8 MiB of scratch and 65536
+ * counters per call (lsa_sparse_read_plan reports a call's needs); larger calls return
+ * LSA_ERR_SIZE and launch nothing. It calls no allocator. The first call on each device
+ * resolves the arrays' addresses, so make it before any stream capture; each call zeroes
+ * the counters it uses; calls share the arrays, so calls that overlap on the GPU race. */
+int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
+                            const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
+                            int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

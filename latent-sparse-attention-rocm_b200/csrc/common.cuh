@@ -199,6 +199,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 #define LSA_ERR_CUDA (-2)
 #define LSA_ERR_TIMEOUT (-3)
 #define LSA_ERR_SHORT (-4)
+#define LSA_ERR_SIZE (-5)
 
 #define LSA_LAUNCH_CHECK()                                    \
     do {                                                      \

@@ -16,6 +16,8 @@
 // of a (row, KV head) - atomic ticket - merges them. With one split the CTA writes the
 // output directly. Every mbarrier wait is bounded (2 s of %globaltimer): on expiry the
 // CTA records LSA_ERR_TIMEOUT in the workspace status word and leaves.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace lsa {
@@ -438,6 +440,79 @@ int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, cons
                     int64_t n_counters, int64_t splits, cudaStream_t stream) {
     return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out, scratch,
                                    scratch_bytes, counters, n_counters, splits, stream);
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation entry
+//
+// Some callers cannot call cudaMalloc at all: an inference server whose device memory is
+// one pre-reserved arena owned by its own allocator, or a plugin host that forbids
+// allocation once serving has started. lsa_sparse_read_noalloc serves them: the split
+// partials and counters of the read live in fixed device arrays of this library instead of
+// caller-provided buffers. The arrays are file-scope __device__ storage, so every GPU that
+// loads the library holds them (8 MiB + 256 KiB) until the process exits.
+namespace lsa {
+
+constexpr int64_t kNoAllocScratchBytes = 8ll << 20;  // split partials (m, l, o)
+constexpr int64_t kNoAllocCounters = 1 << 16;        // tickets + status word
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) int32_t g_noalloc_counters[kNoAllocCounters];
+
+// Host copies of the arrays' device addresses, one entry per device. In host code the
+// array names above are host-side stand-ins, not device addresses; only these may be
+// handed to a kernel.
+struct NoAllocSlot {
+    void* scratch = nullptr;
+    int32_t* counters = nullptr;
+};
+static NoAllocSlot g_noalloc_slots[128];
+static std::mutex g_noalloc_mutex;
+
+static int noalloc_setup(NoAllocSlot* out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return LSA_ERR_CUDA;
+    if (dev < 0 || dev >= 128) return LSA_ERR_ARG;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    NoAllocSlot& slot = g_noalloc_slots[dev];
+    if (slot.scratch == nullptr) {  // first call on this device (the device is current)
+        void* s = nullptr;
+        void* c = nullptr;
+        if (cudaGetSymbolAddress(&s, g_noalloc_scratch) != cudaSuccess) return LSA_ERR_CUDA;
+        if (cudaGetSymbolAddress(&c, g_noalloc_counters) != cudaSuccess) return LSA_ERR_CUDA;
+        slot.scratch = s;
+        slot.counters = static_cast<int32_t*>(c);
+    }
+    *out = slot;
+    return LSA_OK;
+}
+
+}  // namespace lsa
+
+extern "C" {
+
+// lsa_sparse_read without caller buffers. Limits: the plan's scratch must fit 8 MiB and
+// its counters 65536 (lsa_sparse_read_plan reports both); larger calls return
+// LSA_ERR_SIZE and launch nothing. The first call on each device resolves the arrays'
+// addresses (cudaGetSymbolAddress), so make it before any stream capture. Each call
+// zeroes the counters it uses (cudaMemsetAsync) and then launches the read; calls share
+// the arrays, so calls that overlap on the GPU (different streams, or devices sharing a
+// context) race and must be serialised by the caller.
+int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
+                            const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
+                            int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream) {
+    if (Hkv <= 0 || Hq % Hkv || width < 0 || D <= 0) return LSA_ERR_ARG;
+    lsa::ReadPlan p = lsa::plan_read(B * Tq, Hkv, Hq / Hkv, D, width, splits, lsa::num_sms());
+    if (p.scratch_bytes > lsa::kNoAllocScratchBytes || p.counters > lsa::kNoAllocCounters) return LSA_ERR_SIZE;
+    lsa::NoAllocSlot slot;
+    int rc = lsa::noalloc_setup(&slot);
+    if (rc != LSA_OK) return rc;
+    if (cudaMemsetAsync(slot.counters, 0, (size_t)p.counters * sizeof(int32_t), stream) != cudaSuccess)
+        return LSA_ERR_CUDA;
+    return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out,
+                                   slot.scratch, lsa::kNoAllocScratchBytes, slot.counters, lsa::kNoAllocCounters,
+                                   splits, stream);
 }
 
 }  // extern "C"

@@ -19,7 +19,7 @@ LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblsa_b200.so"
 F32, F16, BF16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
-OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_SHORT = 0, -1, -2, -3, -4
+OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_SHORT, ERR_SIZE = 0, -1, -2, -3, -4, -5
 
 _lib = None
 _lock = threading.Lock()
@@ -52,6 +52,7 @@ SIGNATURES = {
     "lsa_position_buckets": (_INT, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "lsa_pair_to_size_workspace": (_I, [_I, _I, _I]),
     "lsa_pair_to_size": (_INT, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P]),
+    "lsa_sparse_read_noalloc": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _I, _P]),
     "lsa_tree_plan": (_INT, [_I, _I, _P, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_tree_select": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P,
                                _I, _P]),
@@ -89,6 +90,8 @@ def check(rc: int, what: str) -> None:
         raise ValueError(f"{what}: arguments rejected by the kernel entry point")
     if rc == ERR_TIMEOUT:
         raise RuntimeError(f"{what}: a bounded device wait expired")
+    if rc == ERR_SIZE:
+        raise ValueError(f"{what}: the call exceeds the fixed no-allocation scratch (8 MiB, 65536 counters)")
     if rc == ERR_SHORT:
         raise ValueError(f"{what}: a cluster block could not reach its bucket count under the cap")
     raise RuntimeError(f"{what}: CUDA launch failed (status {rc})")
