@@ -5,27 +5,43 @@
 // h / (Hq / Hkv)), the ids >= 0 among the first min(length, width) slots are read;
 // s = (q . k) * scale in fp32; fp32 online softmax from a finite -3e38 running max;
 // o = sum p v / l; a row with no listed key gives zeros; duplicates count per occurrence;
-// the output takes q's dtype.
+// the output takes q's dtype. Ids outside [0, Tk) are skipped, never dereferenced.
 //
-// B200 design: split-K flash decoding. One CTA per (row, KV head, split) serves all G
-// query heads of the KV head, so each gathered K/V row is read from HBM once for the
-// group. The CTA's ids are fetched in stages of 64: warp 0 issues one cp.async.bulk
-// (TMA bulk copy) per listed K row and per V row straight into shared memory, completion
-// tracked by an mbarrier (expect_tx bytes), two stages in flight. Each 16-byte lane vector
-// carries 8 elements of a row. Partial (m, l, o) per split go to a workspace; the last CTA
-// of a (row, KV head) - atomic ticket - merges them. With one split the CTA writes the
-// output directly. Every mbarrier wait is bounded (2 s of %globaltimer): on expiry the
-// CTA records LSA_ERR_TIMEOUT in the workspace status word and leaves.
+// B200 design: split-K flash decoding. One CTA (8 warps) per (row, KV head, split) serves
+// all G query heads of the KV head, so each gathered K/V row crosses HBM once per group.
+// The CTA's ids are fetched in stages (128 ids for 16-bit types): every warp issues one
+// cp.async.bulk (TMA bulk copy) per listed K row and V row of its 16 slots straight into
+// shared memory, completion counted by an mbarrier (one expect_tx arrival per warp), two
+// stages in flight; the id and length loads overlap (no dependent round trip). A lane holds
+// 8 elements (one 16-byte vector) of a row; 16 lanes cover a Dh = 128 row.
+// Split partials (m, l, o) merge three ways:
+//   * 1 split: the CTA writes the output;
+//   * <= 16 splits: the splits of a (row, KV head) form one thread-block cluster and merge
+//     through distributed shared memory - every CTA combines a slice of the outputs;
+//   * more: partials go to global scratch and the last CTA (atomic ticket) merges them.
+// Launches carry programmatic stream serialization: the kernel calls griddepcontrol.wait
+// before its first global read, so it may be resident before its producer finishes.
+// Every mbarrier wait is bounded (2 s of %globaltimer); on expiry the CTA records
+// LSA_ERR_TIMEOUT in the status counter and leaves after a second bounded wait.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace lsa {
 
-constexpr int kStageIds = 64;      // ids per pipeline stage
-constexpr int kReadThreads = 128;  // 4 warps
+constexpr int kReadThreads = 256;  // 8 warps
+constexpr int kMaxClusterSplits = 16;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegBig = -3.0e38f;
+
+template <typename T>
+struct StageIds {
+    static constexpr int value = sizeof(T) == 4 ? 64 : 128;
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -71,6 +87,64 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Four 8x8 b16 matrices from shared memory (lane l addresses row l & 7 of matrix l >> 3).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// D[16x8] += A[16x16] B[16x8], fp32 accumulate; A, B both bf16 or both fp16.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two fp32 values as one register of the 16-bit type (lo in the low half).
+template <typename T> __device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<float>(float, float) { return 0u; }
+template <>
+__device__ __forceinline__ void mma16816<float>(float (&)[4], uint32_t, uint32_t, uint32_t, uint32_t, uint32_t,
+                                                uint32_t) {}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+enum Combine : int { kSingle = 0, kCluster = 1, kTicket = 2 };
+
 struct ReadArgs {
     const void* q;
     const void* k;
@@ -78,213 +152,342 @@ struct ReadArgs {
     const int32_t* ids;
     const int32_t* lengths;
     void* out;
-    float* part_o;   // [R*Hkv, splits, G, D]
+    float* part_o;   // [R*Hkv, splits, G, D]   (ticket combine)
     float* part_ml;  // [R*Hkv, splits, G, 2]
     int32_t* tickets;
     int32_t* status;
     int64_t Tq, Tk;
-    int Hq, Hkv, G, width, splits, span;
+    int Hq, Hkv, G, width, splits, span, combine;
     float scale_log2;  // scale * log2(e)
 };
 
 template <typename T, int D, int GMAX>
 __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
-    constexpr int LPR = D / 8;         // lanes per key row (8 elements per lane)
-    constexpr int GPW = 32 / LPR;      // key rows per warp step
-    constexpr int NG = 4 * GPW;        // row groups in the CTA
-    constexpr int ROWB = D * sizeof(T);
-    constexpr int STAGE_BYTES = kStageIds * ROWB;
+    constexpr int STAGE = StageIds<T>::value;
+    constexpr int LPR = D / 8;          // lanes per key row (8 elements per lane)
+    constexpr int GPW = 32 / LPR;       // key rows per warp step
+    constexpr int NW = kReadThreads / 32;
+    constexpr int NG = NW * GPW;        // row groups in the CTA
+    constexpr int PER = STAGE / NG;     // slots of a group in a stage
+    constexpr bool MMA = sizeof(T) == 2;      // tensor-core path for 16-bit inputs
+    constexpr int NGE = MMA ? NW : NG;        // partial-state owners merged at the end
+    constexpr int ROWS = MMA ? D + 8 : D;     // smem row stride (elements): +16 B keeps ldmatrix conflict-free
+    constexpr int ROWB = D * sizeof(T);       // bytes copied per row
+    constexpr int STAGE_BYTES = STAGE * ROWS * (int)sizeof(T);
+    constexpr int IDW = STAGE / NW;     // id slots a warp issues per stage
+    static_assert(2 * IDW <= 32, "a warp issues the K and V rows of its slots in one pass");
     extern __shared__ __align__(128) unsigned char smem[];
-    T* sK = reinterpret_cast<T*>(smem);                      // [2][kStageIds][D]
-    T* sV = reinterpret_cast<T*>(smem + 2 * STAGE_BYTES);    // [2][kStageIds][D]
+    T* sK = reinterpret_cast<T*>(smem);                    // [2][STAGE][D]
+    T* sV = reinterpret_cast<T*>(smem + 2 * STAGE_BYTES);  // [2][STAGE][D]
     __shared__ __align__(8) uint64_t bars[2];
+    __shared__ unsigned char sflag[2 * STAGE];              // slot listed and in range
     __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int grp = warp * GPW + lane / LPR;  // row group of this lane
-    const int lg = lane % LPR;                // lane within the group
-    const int rh = blockIdx.x / a.splits;     // row * Hkv + kv head
+    const int grp = warp * GPW + lane / LPR;
+    const int lg = lane % LPR;
+    const int rh = blockIdx.x / a.splits;  // row * Hkv + kv head
     const int split = blockIdx.x % a.splits;
     const int64_t row = rh / a.Hkv;
     const int h = rh % a.Hkv;
     const int64_t b = row / a.Tq;
     const int G = a.G;
 
-    int len = a.lengths[row];
-    len = len < 0 ? 0 : (len > a.width ? a.width : len);
+    if (tid == 0) {
+        mbar_init(&bars[0], NW);  // one expect_tx arrival per warp per stage
+        mbar_init(&bars[1], NW);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    pdl_wait();  // inputs produced by the previous kernel are visible past this point
+    pdl_trigger();
+
     const int s0 = split * a.span;
-    const int s1 = min(s0 + a.span, len);
-    const int n_ids = s1 > s0 ? s1 - s0 : 0;
-    const int n_stages = (n_ids + kStageIds - 1) / kStageIds;
     const int32_t* idrow = a.ids + row * a.width;
     const T* kbase = reinterpret_cast<const T*>(a.k) + (b * a.Tk * a.Hkv + h) * D;
     const T* vbase = reinterpret_cast<const T*>(a.v) + (b * a.Tk * a.Hkv + h) * D;
     const int64_t tstride = (int64_t)a.Hkv * D;  // elements between consecutive positions
+    // Every warp issues the copies of its own IDW slots per stage: lanes [0, IDW) the K rows,
+    // lanes [IDW, 2 IDW) the V rows of the same slots.
+    const bool issuer = lane < 2 * IDW;
+    const bool is_v = lane >= IDW;
+    const int my_slot = warp * IDW + (lane % IDW);
+    auto load_id = [&](int stage) -> int {  // needs no length: loads overlap the length load
+        int at = s0 + stage * STAGE + my_slot;
+        return (issuer && at < s0 + a.span && at < a.width) ? idrow[at] : -1;
+    };
+    int id0 = load_id(0), id1 = load_id(1);
+    int len = a.lengths[row];
+    len = len < 0 ? 0 : (len > a.width ? a.width : len);
+    const int s1 = min(s0 + a.span, len);
+    const int n_ids = s1 > s0 ? s1 - s0 : 0;
+    const int n_stages = (n_ids + STAGE - 1) / STAGE;
 
-    if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-
-    // warp 0 issues one stage: bulk copies of every listed K and V row of the stage
-    auto issue = [&](int stage) {
+    auto issue = [&](int stage, int id) {
         int buf = stage & 1;
-        int base = s0 + stage * kStageIds;
-        int cnt = min(kStageIds, s1 - base);
-        int idv[2];
-        bool ok[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            int j = lane + 32 * u;
-            idv[u] = j < cnt ? idrow[base + j] : -1;
-            ok[u] = idv[u] >= 0 && idv[u] < a.Tk;
-        }
-        uint32_t n = __popc(__ballot_sync(0xFFFFFFFFu, ok[0])) + __popc(__ballot_sync(0xFFFFFFFFu, ok[1]));
-        if (lane == 0) mbar_expect_tx_arrive(&bars[buf], n * 2u * ROWB);
+        int at = s0 + stage * STAGE + my_slot;
+        bool ok = issuer && at < s1 && id >= 0 && id < a.Tk;
+        uint32_t n = __popc(__ballot_sync(0xFFFFFFFFu, ok));
+        if (lane == 0) mbar_expect_tx_arrive(&bars[buf], n * ROWB);
+        if (issuer && !is_v) sflag[buf * STAGE + my_slot] = ok ? 1 : 0;
         __syncwarp();
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (ok[u]) {
-                int j = lane + 32 * u;
-                bulk_g2s(sK + ((size_t)buf * kStageIds + j) * D, kbase + (int64_t)idv[u] * tstride, ROWB, &bars[buf]);
-                bulk_g2s(sV + ((size_t)buf * kStageIds + j) * D, vbase + (int64_t)idv[u] * tstride, ROWB, &bars[buf]);
-            }
+        if (ok) {
+            T* dst = (is_v ? sV : sK) + ((size_t)buf * STAGE + my_slot) * ROWS;
+            const T* src = (is_v ? vbase : kbase) + (int64_t)id * tstride;
+            bulk_g2s(dst, src, ROWB, &bars[buf]);
         }
     };
 
-    if (warp == 0) {
-        if (n_stages > 0) issue(0);
-        if (n_stages > 1) issue(1);
-    }
-
-    // q of the group's heads, this lane's 8 dims, pre-scaled into the log2 domain
-    float qr[GMAX][8];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-        if (g < G) {
-            const T* qp = reinterpret_cast<const T*>(a.q) + ((row * a.Hq) + h * G + g) * D + lg * 8;
-            load8<T>(qp, qr[g]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qr[g][e] *= a.scale_log2;
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qr[g][e] = 0.0f;
-        }
-    }
-    float m[GMAX], l[GMAX], acc[GMAX][8];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-        m[g] = kNegBig;
-        l[g] = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
-    }
+    if (n_stages > 0) issue(0, id0);
+    if (n_stages > 1) issue(1, id1);
+    __syncthreads();  // slot flags visible to every group
 
     bool failed = false;
-    for (int st = 0; st < n_stages; ++st) {
-        int buf = st & 1;
-        bool ok = mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
-        if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
-            // give copies still in flight a second bounded window before the CTA exits
-            if (tid == 0) mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
-            __syncthreads();
-            failed = true;
-            break;
+    float* red = reinterpret_cast<float*>(smem);  // [NGE][GMAX][D] group partials (after the loop)
+    float* redml = red + NGE * GMAX * D;          // [NGE][GMAX][2]
+    float* po = redml + NGE * GMAX * 2;           // [GMAX][D]  the CTA's partial
+    float* pml = po + GMAX * D;                   // [GMAX][2]
+
+    if constexpr (MMA) {
+        // Tensor-core path (16-bit inputs): warp w owns slots [16 w, 16 w + 16) of a stage.
+        // S = q K^T as mma.m16n8k16 with the query heads as M (rows >= G are zero), the
+        // scores stay in registers and become the P operand of O += P V (FA2 fragment reuse).
+        const int gq = lane >> 2, tq = lane & 3;
+        constexpr int DC = D / 16;  // k16 chunks over the head dim
+        constexpr int NT = D / 8;   // n8 output tiles over the head dim
+        uint32_t qa[DC][2];         // rows gq of the A operand (rows gq + 8 are zero padding)
+#pragma unroll
+        for (int dc = 0; dc < DC; ++dc) {
+            const T* qp = reinterpret_cast<const T*>(a.q) + ((row * a.Hq) + h * G + gq) * D + dc * 16 + 2 * tq;
+            qa[dc][0] = gq < G ? *reinterpret_cast<const uint32_t*>(qp) : 0u;
+            qa[dc][1] = gq < G ? *reinterpret_cast<const uint32_t*>(qp + 8) : 0u;
         }
-        int base = s0 + st * kStageIds;
-        int cnt = min(kStageIds, s1 - base);
-        constexpr int PER = kStageIds / NG;  // slots of this group in the stage
-        float s[PER][GMAX];
-        bool kept[PER];
+        float o[NT][4];
 #pragma unroll
-        for (int u = 0; u < PER; ++u) {
-            int j = grp + NG * u;
-            int id = j < cnt ? idrow[base + j] : -1;
-            kept[u] = id >= 0 && id < a.Tk;
+        for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+        float mrow = kNegBig, lrow = 0.0f;  // row gq (this thread's share of l; quad-summed at the end)
+        for (int st = 0; st < n_stages; ++st) {
+            int buf = st & 1;
+            bool ok = mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+            if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
+                if (tid == 0) mbar_wait_bounded(&bars[buf], (st >> 1) & 1);  // copies in flight
+                __syncthreads();
+                failed = true;
+                break;
+            }
+            const int kb = warp * 16;  // first slot of this warp
+            const unsigned char* fl = sflag + buf * STAGE + kb;
+            bool any = __any_sync(0xFFFFFFFFu, lane < 16 && fl[lane & 15]);
+            if (any) {
+                const uint32_t kaddr = smem_u32(sK + ((size_t)buf * STAGE + kb) * ROWS);
+                const uint32_t vaddr = smem_u32(sV + ((size_t)buf * STAGE + kb) * ROWS);
+                float sc[2][4];
 #pragma unroll
-            for (int g = 0; g < GMAX; ++g) s[u][g] = kNegBig;
-            if (kept[u]) {
-                float kv[8];
-                load8<T>(sK + ((size_t)buf * kStageIds + j) * D + lg * 8, kv);
+                for (int j = 0; j < 2; ++j) {
+                    sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
 #pragma unroll
-                for (int g = 0; g < GMAX; ++g) {
-                    float p = 0.0f;
+                    for (int q4 = 0; q4 < DC / 2; ++q4) {  // 4 dim blocks of 8 per ldmatrix.x4
+                        uint32_t b0, b1, b2, b3;
+                        uint32_t addr = kaddr + ((8 * j + (lane & 7)) * ROWS + (4 * q4 + (lane >> 3)) * 8) * 2;
+                        ldsm_x4(addr, b0, b1, b2, b3);
+                        mma16816<T>(sc[j], qa[2 * q4][0], 0u, qa[2 * q4][1], 0u, b0, b1);
+                        mma16816<T>(sc[j], qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
+                    }
+                }
+                // scores of row gq for keys 8j + 2tq + {0, 1}; unlisted slots never count
+                float sv[4];
+                float mx = kNegBig;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) p = fmaf(qr[g][e], kv[e], p);
-                    s[u][g] = p;
+                for (int j = 0; j < 2; ++j)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        bool valid = fl[8 * j + 2 * tq + e] != 0;
+                        float v = valid ? sc[j][e] * a.scale_log2 : -INFINITY;
+                        sv[2 * j + e] = v;
+                        mx = fmaxf(mx, v);
+                    }
+                mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+                float mnew = fmaxf(mrow, mx);
+                float alpha = exp2f(mrow - mnew);
+                mrow = mnew;
+                float p[4];
+                float psum = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    p[i] = exp2f(sv[i] - mnew);
+                    psum += p[i];
+                }
+                lrow = lrow * alpha + psum;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    o[nt][0] *= alpha;
+                    o[nt][1] *= alpha;
+                }
+                uint32_t pa0 = pack2<T>(p[0], p[1]), pa2 = pack2<T>(p[2], p[3]);
+                // V rows of unlisted slots hold stale shared memory: zero their fragment halves
+                // (b0/b2 carry keys 2tq, 2tq + 1; b1/b3 keys 8 + 2tq, 9 + 2tq) so 0 * garbage
+                // cannot turn into NaN inside the MMA
+                const uint32_t vm0 = (fl[2 * tq] ? 0x0000FFFFu : 0u) | (fl[2 * tq + 1] ? 0xFFFF0000u : 0u);
+                const uint32_t vm1 = (fl[8 + 2 * tq] ? 0x0000FFFFu : 0u) | (fl[9 + 2 * tq] ? 0xFFFF0000u : 0u);
+#pragma unroll
+                for (int np = 0; np < NT / 2; ++np) {
+                    uint32_t b0, b1, b2, b3;
+                    int key = (lane & 7) + 8 * ((lane >> 3) & 1);
+                    int dblk = 2 * np + (lane >> 4);
+                    ldsm_x4_t(vaddr + (key * ROWS + dblk * 8) * 2, b0, b1, b2, b3);
+                    mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
+                    mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
+                }
+            }
+            __syncthreads();  // every warp is done with this buffer
+            if (st + 2 < n_stages) issue(st + 2, load_id(st + 2));
+        }
+        if (!failed) {
+            lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 1);
+            lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 2);
+            if (gq < G) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    red[(warp * GMAX + gq) * D + nt * 8 + 2 * tq] = o[nt][0];
+                    red[(warp * GMAX + gq) * D + nt * 8 + 2 * tq + 1] = o[nt][1];
+                }
+                if (tq == 0) {
+                    redml[(warp * GMAX + gq) * 2] = mrow;
+                    redml[(warp * GMAX + gq) * 2 + 1] = lrow;
                 }
             }
         }
-        // reduce the partial dots across the LPR lanes of each group
-#pragma unroll
-        for (int u = 0; u < PER; ++u)
-#pragma unroll
-            for (int g = 0; g < GMAX; ++g)
-#pragma unroll
-                for (int off = LPR / 2; off >= 1; off >>= 1) s[u][g] += __shfl_xor_sync(0xFFFFFFFFu, s[u][g], off);
+    } else {
+        // CUDA-core path (fp32 inputs): 16 lanes hold a row, 8 elements each.
+        float qr[GMAX][8];
 #pragma unroll
         for (int g = 0; g < GMAX; ++g) {
-            float mx = m[g];
+            if (g < G) {
+                const T* qp = reinterpret_cast<const T*>(a.q) + ((row * a.Hq) + h * G + g) * D + lg * 8;
+                load8<T>(qp, qr[g]);
 #pragma unroll
-            for (int u = 0; u < PER; ++u)
-                if (kept[u]) mx = fmaxf(mx, s[u][g]);
-            float alpha = exp2f(m[g] - mx);
-            l[g] *= alpha;
+                for (int e = 0; e < 8; ++e) qr[g][e] *= a.scale_log2;
+            } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
-            m[g] = mx;
-        }
-#pragma unroll
-        for (int u = 0; u < PER; ++u) {
-            if (!kept[u]) continue;
-            int j = grp + NG * u;
-            float vv[8];
-            load8<T>(sV + ((size_t)buf * kStageIds + j) * D + lg * 8, vv);
-#pragma unroll
-            for (int g = 0; g < GMAX; ++g) {
-                float p = exp2f(s[u][g] - m[g]);
-                l[g] += p;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vv[e], acc[g][e]);
+                for (int e = 0; e < 8; ++e) qr[g][e] = 0.0f;
             }
         }
-        __syncthreads();  // every group is done with this buffer
-        if (warp == 0 && st + 2 < n_stages) issue(st + 2);
+        float m[GMAX], l[GMAX], acc[GMAX][8];
+#pragma unroll
+        for (int g = 0; g < GMAX; ++g) {
+            m[g] = kNegBig;
+            l[g] = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+        }
+        for (int st = 0; st < n_stages; ++st) {
+            int buf = st & 1;
+            bool ok = mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+            if (__syncthreads_or(!ok)) {
+                if (tid == 0) mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+                __syncthreads();
+                failed = true;
+                break;
+            }
+            float s[PER][GMAX];
+            bool kept[PER];
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                int j = grp + NG * u;
+                kept[u] = sflag[buf * STAGE + j] != 0;
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g) s[u][g] = kNegBig;
+                if (kept[u]) {
+                    float kv[8];
+                    load8<T>(sK + ((size_t)buf * STAGE + j) * ROWS + lg * 8, kv);
+#pragma unroll
+                    for (int g = 0; g < GMAX; ++g) {
+                        float p = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) p = fmaf(qr[g][e], kv[e], p);
+                        s[u][g] = p;
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u)
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g)
+#pragma unroll
+                    for (int off = LPR / 2; off >= 1; off >>= 1)
+                        s[u][g] += __shfl_xor_sync(0xFFFFFFFFu, s[u][g], off);
+#pragma unroll
+            for (int g = 0; g < GMAX; ++g) {
+                float mx = m[g];
+#pragma unroll
+                for (int u = 0; u < PER; ++u)
+                    if (kept[u]) mx = fmaxf(mx, s[u][g]);
+                float alpha = exp2f(m[g] - mx);
+                l[g] *= alpha;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
+                m[g] = mx;
+            }
+#pragma unroll
+            for (int u = 0; u < PER; ++u) {
+                if (!kept[u]) continue;
+                int j = grp + NG * u;
+                float vv[8];
+                load8<T>(sV + ((size_t)buf * STAGE + j) * ROWS + lg * 8, vv);
+#pragma unroll
+                for (int g = 0; g < GMAX; ++g) {
+                    float p = exp2f(s[u][g] - m[g]);
+                    l[g] += p;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[g][e] = fmaf(p, vv[e], acc[g][e]);
+                }
+            }
+            __syncthreads();
+            if (st + 2 < n_stages) issue(st + 2, load_id(st + 2));
+        }
+        if (!failed) {
+#pragma unroll
+            for (int g = 0; g < GMAX; ++g) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) red[(grp * GMAX + g) * D + lg * 8 + e] = acc[g][e];
+                if (lg == 0) {
+                    redml[(grp * GMAX + g) * 2] = m[g];
+                    redml[(grp * GMAX + g) * 2 + 1] = l[g];
+                }
+            }
+        }
     }
     if (failed) {
-        if (lane == 0) atomicExch(a.status, LSA_ERR_TIMEOUT);
+        if (tid == 0) atomicExch(a.status, LSA_ERR_TIMEOUT);
+        if (a.combine == kCluster) cg::this_cluster().sync();  // peers reach both barriers below
+        if (a.combine == kCluster) cg::this_cluster().sync();
         return;
     }
 
-    // merge the NG row groups of the CTA (stage buffers are free now)
-    float* red = reinterpret_cast<float*>(smem);  // [NG][GMAX][D] then m,l [NG][GMAX][2]
-    float* redml = red + NG * GMAX * D;
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) red[(grp * GMAX + g) * D + lg * 8 + e] = acc[g][e];
-        if (lg == 0) {
-            redml[(grp * GMAX + g) * 2] = m[g];
-            redml[(grp * GMAX + g) * 2 + 1] = l[g];
-        }
-    }
+    // merge the NGE row groups of the CTA
     __syncthreads();
-    const bool single = a.splits == 1;
     for (int o = tid; o < G * D; o += kReadThreads) {
         int g = o / D, e = o % D;
         float M = kNegBig;
-        for (int r = 0; r < NG; ++r) M = fmaxf(M, redml[(r * GMAX + g) * 2]);
+#pragma unroll 4
+        for (int r = 0; r < NGE; ++r) M = fmaxf(M, redml[(r * GMAX + g) * 2]);
         float L = 0.0f, O = 0.0f;
-        for (int r = 0; r < NG; ++r) {
+#pragma unroll 4
+        for (int r = 0; r < NGE; ++r) {
             float f = exp2f(redml[(r * GMAX + g) * 2] - M);
             L += redml[(r * GMAX + g) * 2 + 1] * f;
             O += red[(r * GMAX + g) * D + e] * f;
         }
-        if (single) {
+        if (a.combine == kSingle) {
             float val = L > 0.0f ? O / L : 0.0f;
             reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
+        } else if (a.combine == kCluster) {
+            po[g * D + e] = O;
+            if (e == 0) {
+                pml[g * 2] = M;
+                pml[g * 2 + 1] = L;
+            }
         } else {
             int64_t pidx = ((int64_t)rh * a.splits + split) * G + g;
             a.part_o[pidx * D + e] = O;
@@ -294,7 +497,45 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
             }
         }
     }
-    if (single) return;
+    if (a.combine == kSingle) return;
+
+    if (a.combine == kCluster) {
+        // every CTA of the cluster merges a slice of the outputs from all ranks' partials
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        const int S = a.splits;
+        const int total = G * D;
+        const int chunk = (total + S - 1) / S;
+        const int o0 = split * chunk;
+        for (int o = o0 + tid; o < min(o0 + chunk, total); o += kReadThreads) {
+            int g = o / D, e = o % D;
+            float mr[kMaxClusterSplits];
+            float M = kNegBig;
+#pragma unroll
+            for (int r = 0; r < kMaxClusterSplits; ++r) {
+                if (r < S) {
+                    const float* peer = cluster.map_shared_rank(pml, r);
+                    mr[r] = peer[g * 2];
+                    M = fmaxf(M, mr[r]);
+                }
+            }
+            float L = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kMaxClusterSplits; ++r) {
+                if (r < S) {
+                    const float* peer_ml = cluster.map_shared_rank(pml, r);
+                    const float* peer_o = cluster.map_shared_rank(po, r);
+                    float f = exp2f(mr[r] - M);
+                    L += peer_ml[g * 2 + 1] * f;
+                    O += peer_o[g * D + e] * f;
+                }
+            }
+            float val = L > 0.0f ? O / L : 0.0f;
+            reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
+        }
+        cluster.sync();  // keep this CTA's partial alive until every peer has read it
+        return;
+    }
 
     __threadfence();
     __syncthreads();
@@ -306,25 +547,37 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    // stage the split weights, then every output sums its splits with independent loads
+    float* wts = red;  // [splits][G] weights, then [G] totals
+    float* tot = red + a.splits * G;
+    for (int i = tid; i < a.splits * G; i += kReadThreads) wts[i] = __ldcg(a.part_ml + ((int64_t)rh * a.splits * G + i) * 2);
+    __syncthreads();
+    if (tid < G) {
+        float M = kNegBig;
+        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, wts[sp * G + tid]);
+        float L = 0.0f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+            float f = exp2f(wts[sp * G + tid] - M);
+            L += __ldcg(a.part_ml + (((int64_t)rh * a.splits + sp) * G + tid) * 2 + 1) * f;
+            wts[sp * G + tid] = f;
+        }
+        tot[tid] = L;
+    }
+    __syncthreads();
     for (int o = tid; o < G * D; o += kReadThreads) {
         int g = o / D, e = o % D;
-        float M = kNegBig;
+        float O = 0.0f;
+#pragma unroll 8
         for (int sp = 0; sp < a.splits; ++sp)
-            M = fmaxf(M, __ldcg(a.part_ml + (((int64_t)rh * a.splits + sp) * G + g) * 2));
-        float L = 0.0f, O = 0.0f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-            int64_t pidx = ((int64_t)rh * a.splits + sp) * G + g;
-            float f = exp2f(__ldcg(a.part_ml + pidx * 2) - M);
-            L += __ldcg(a.part_ml + pidx * 2 + 1) * f;
-            O += __ldcg(a.part_o + pidx * D + e) * f;
-        }
+            O += wts[sp * G + g] * __ldcg(a.part_o + (((int64_t)rh * a.splits + sp) * G + g) * D + e);
+        float L = tot[g];
         float val = L > 0.0f ? O / L : 0.0f;
         reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
     }
 }
 
 struct ReadPlan {
-    int splits, span;
+    int splits, span, combine;
     int64_t part_o_bytes, part_ml_bytes, scratch_bytes, counters;
 };
 
@@ -336,24 +589,82 @@ static int num_sms() {
 
 static int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
 
-// splits: CTAs per (row, KV head). Auto (splits_req <= 0): enough CTAs for two per SM,
-// at most one split per 16 ids of the width.
+template <typename T, int D, int GMAX>
+static constexpr int read_smem_bytes() {
+    constexpr int STAGE = StageIds<T>::value;
+    constexpr bool MMA = sizeof(T) == 2;
+    constexpr int NG = (kReadThreads / 32) * (32 / (D / 8));
+    constexpr int NGE = MMA ? kReadThreads / 32 : NG;
+    constexpr int ROWS = MMA ? D + 8 : D;
+    constexpr int stage_bytes = 4 * STAGE * ROWS * (int)sizeof(T);
+    constexpr int red_bytes = (NGE * GMAX * D + NGE * GMAX * 2 + GMAX * D + GMAX * 2) * 4;
+    return stage_bytes > red_bytes ? stage_bytes : red_bytes;
+}
+
+// How many clusters of each size (1..16 read CTAs) one device holds at once, probed once
+// per device on the heaviest instantiation. A size the GPCs cannot place reports 0.
+static const int* cluster_capacity() {
+    static int table[128][kMaxClusterSplits + 1];
+    static bool probed[128] = {false};
+    static std::mutex m;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) dev = 0;
+    std::lock_guard<std::mutex> lock(m);
+    if (!probed[dev]) {
+        auto kern = sparse_read_kernel<__nv_bfloat16, 128, 8>;
+        constexpr int smem = read_smem_bytes<__nv_bfloat16, 128, 8>();
+        bool ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+                  cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+        for (int c = 0; c <= kMaxClusterSplits; ++c) {
+            table[dev][c] = 0;
+            if (!ok || c < 1) continue;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(c);
+            cfg.blockDim = dim3(kReadThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr;
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = c;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess) table[dev][c] = n;
+        }
+        cudaGetLastError();  // a refused probe leaves no sticky error
+        probed[dev] = true;
+    }
+    return table[dev];
+}
+
+// splits: CTAs per (row, KV head). Auto (splits_req <= 0): about four CTAs per SM over the
+// whole launch, at least 128 ids per split, at most one cluster. A count above the cluster
+// limit merges through the ticket path.
 static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t width, int64_t splits_req, int sms) {
     ReadPlan p;
+    const int* cap = cluster_capacity();
     int64_t units = R * Hkv;
-    int64_t max_splits = (width + 15) / 16;
-    if (max_splits < 1) max_splits = 1;
     int64_t s = splits_req;
     if (s <= 0) {
-        int64_t target = 2 * (int64_t)sms;
+        int64_t target = 4 * (int64_t)sms;
         s = (target + units - 1) / (units > 0 ? units : 1);
+        int64_t by_len = (width + 127) / 128;
+        if (s > by_len) s = by_len;
+        if (s > kMaxClusterSplits) s = kMaxClusterSplits;
+        // the largest cluster size whose clusters all fit the device at once (portable 8 floor)
+        while (s > 8 && cap[s] < units) --s;
     }
+    int64_t max_splits = width > 0 ? width : 1;
     if (s > max_splits) s = max_splits;
     if (s < 1) s = 1;
     p.splits = (int)s;
     p.span = (int)((width + s - 1) / s);
-    p.part_o_bytes = s > 1 ? round256(units * s * G * D * 4) : 0;
-    p.part_ml_bytes = s > 1 ? round256(units * s * G * 2 * 4) : 0;
+    bool placeable = s <= kMaxClusterSplits && (s <= 8 || cap[s] > 0);
+    p.combine = s == 1 ? kSingle : (placeable ? kCluster : kTicket);
+    bool scratch = p.combine == kTicket;
+    p.part_o_bytes = scratch ? round256(units * s * G * D * 4) : 0;
+    p.part_ml_bytes = scratch ? round256(units * s * G * 2 * 4) : 0;
     p.scratch_bytes = p.part_o_bytes + p.part_ml_bytes;
     p.counters = units + 1;  // one ticket per (row, KV head) + the status word
     return p;
@@ -361,12 +672,33 @@ static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t 
 
 template <typename T, int D, int GMAX>
 static int launch_read(const ReadArgs& a, int64_t ctas, cudaStream_t st) {
-    constexpr int smem = 4 * kStageIds * D * (int)sizeof(T);
+    constexpr int smem = read_smem_bytes<T, D, GMAX>();
     auto kern = sparse_read_kernel<T, D, GMAX>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return LSA_ERR_CUDA;
-    kern<<<(unsigned)ctas, kReadThreads, smem, st>>>(a);
-    LSA_LAUNCH_CHECK();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3(kReadThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    int n = 0;
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+    if (a.combine == kCluster) {
+        if (a.splits > 8 &&
+            cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+            return LSA_ERR_CUDA;
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = (unsigned)a.splits;
+        attrs[n].val.clusterDim.y = 1;
+        attrs[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return LSA_ERR_CUDA;
     return LSA_OK;
 }
 
@@ -408,7 +740,7 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     a.status = counters + R * Hkv;
     a.Tq = Tq; a.Tk = Tk;
     a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.G = (int)G; a.width = (int)width;
-    a.splits = p.splits; a.span = p.span;
+    a.splits = p.splits; a.span = p.span; a.combine = p.combine;
     a.scale_log2 = scale * kLog2e;
     int64_t ctas = R * Hkv * p.splits;
     if (dtype == kBF16) return dispatch_d<__nv_bfloat16>(a, (int)D, ctas, stream);

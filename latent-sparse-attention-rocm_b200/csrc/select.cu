@@ -228,11 +228,105 @@ struct GlobalKeysCg {
     __device__ int64_t operator()(int i) const { return i < count ? __ldcg(row + i) : kEmpty; }
 };
 
-// One launch from index queries to read lists. grid = (chunks, R), block = 256.
-// Workspace: keys [R, N] int64 and tickets [R] int32 (zero at allocation; the last CTA of a
-// row resets its ticket, so the launch can be replayed, e.g. from a CUDA graph).
+constexpr int kFusedThreads = 512;
+constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Descending bitonic sort of one key per thread across the block (blockDim.x a power of
+// two); returns the key of rank threadIdx.x. Strides below 32 exchange by warp shuffles,
+// larger strides through shared memory (xchg: blockDim.x int64).
+__device__ __forceinline__ int64_t block_bitonic_desc_regs(int64_t x, int64_t* xchg) {
+    const int tid = threadIdx.x, n = blockDim.x;
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            int64_t y;
+            if (j >= 32) {
+                xchg[tid] = x;
+                __syncthreads();
+                y = xchg[tid ^ j];
+                __syncthreads();
+            } else {
+                y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+            }
+            bool lower = (tid & j) == 0;
+            bool desc = (tid & k) == 0;
+            x = (lower == desc) ? (x > y ? x : y) : (x < y ? x : y);
+        }
+    }
+    return x;
+}
+
+// The walk of expand_row with every picked bucket's member row staged in shared memory
+// first (one memory round trip), then one block scan over all (pick, member) slots.
+// Requires P * cap <= kMemberPrefetch; mem holds that many int32.
+__device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t* __restrict__ members,
+                                      int64_t member_rows, int cap, int64_t pos, int window, int sink, int top_k,
+                                      int32_t* __restrict__ out, int width, int32_t* length_out, int* scan_smem,
+                                      int* mem) {
+    int64_t ws = pos + 1 - window;
+    if (ws < 0) ws = 0;
+    const int total = P * cap;
+    // every member load of this thread is issued before any is consumed: one round trip
+    constexpr int kMaxPer = kMemberPrefetch / kFusedThreads;
+    int vals[kMaxPer];
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+        int s = threadIdx.x + i * blockDim.x;
+        vals[i] = -1;
+        if (s < total) {
+            int p = s / cap, m = s - p * cap;
+            int b = key_bucket(picks[p]);
+            if (b >= 0 && b < member_rows) vals[i] = __ldg(members + (int64_t)b * cap + m);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+        int s = threadIdx.x + i * blockDim.x;
+        if (s < total) {
+            int v = vals[i];
+            mem[s] = (v < sink || v >= ws) ? -1 : v;
+        }
+    }
+    __syncthreads();
+    const int spt = (total + blockDim.x - 1) / blockDim.x;
+    const int first = threadIdx.x * spt;
+    int cnt = 0;
+    for (int i = 0; i < spt; ++i) {
+        int s = first + i;
+        cnt += (s < total && mem[s] >= 0);
+    }
+    int filled;
+    int at = block_exclusive_scan(cnt, scan_smem, &filled);
+    for (int i = 0; i < spt; ++i) {
+        int s = first + i;
+        if (s < total && mem[s] >= 0) {
+            if (at < top_k) out[at] = mem[s];
+            ++at;
+        }
+    }
+    if (filled > top_k) filled = top_k;
+    int nwin = (int)(pos - ws + 1);
+    if (nwin < 0) nwin = 0;
+    int nsink = (int)(sink < ws ? sink : ws);
+    for (int i = threadIdx.x; i < width - filled; i += blockDim.x) {
+        int j = filled + i, v = -1;
+        if (i < nwin) v = (int)(ws + i);
+        else if (i < nwin + nsink) v = i - nwin;
+        out[j] = v;
+    }
+    if (threadIdx.x == 0) *length_out = filled + nwin + nsink;
+}
+
+// One launch from index queries to read lists. grid = (chunks, R), block = 512: every
+// warp scores one visible column; the last CTA of a row (atomic ticket) orders the row's
+// packed keys (register bitonic up to 512 keys) and walks the expansion.
+// Scratch: keys [R, N] int64; counters: tickets [R] int32 (zero before the first launch; the
+// last CTA of a row resets its ticket, so launches replay, e.g. from a CUDA graph).
+// Launched with programmatic stream serialization: griddepcontrol.wait precedes every read.
 template <typename TQ, typename TC, int CHUNKS>
-__global__ void __launch_bounds__(256) select_fused_kernel(
+__global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d,
     const int32_t* __restrict__ positions, int64_t block, int64_t bpb, int cols_per_cta, int top_p,
     const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
@@ -240,13 +334,13 @@ __global__ void __launch_bounds__(256) select_fused_kernel(
     extern __shared__ int64_t sbuf[];
     __shared__ int scan_smem[33];
     __shared__ int is_last;
+    pdl_wait();
+    pdl_trigger();
     int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int64_t pos = positions[r];
-    int64_t vis = pos / block * bpb;
-    int count = (int)(vis < N ? vis : N);
-    if (count < 0) count = 0;
+    // score the grid's columns without waiting for the row's position: the last CTA masks
+    // the columns past the row's visible count (the grid covers the widest row)
     int64_t c0 = (int64_t)blockIdx.x * cols_per_cta;
-    int64_t c1 = min(c0 + cols_per_cta, (int64_t)count);
+    int64_t c1 = min(c0 + cols_per_cta, N);
     if (c0 < c1) {
         int nchunks = d >> 3;
         float x[CHUNKS][8];
@@ -270,11 +364,21 @@ __global__ void __launch_bounds__(256) select_fused_kernel(
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    int64_t pos = positions[r];
+    int64_t vis = pos / block * bpb;
+    int count = (int)(vis < N ? vis : N);
+    if (count < 0) count = 0;
     int k = (int)min((int64_t)top_p, N);
     GlobalKeysCg loader{ws_keys + r * N, count};
     int n2 = next_pow2(max(count, 1));
     int64_t* picks = sbuf;  // sorted keys live at the front of the buffer
-    if (n2 <= kSortCap) {
+    if (count <= (int)blockDim.x) {
+        int64_t x = block_bitonic_desc_regs(loader((int)threadIdx.x), sbuf);
+        __syncthreads();  // the exchange buffer becomes the picks
+        if ((int)threadIdx.x < k) picks[threadIdx.x] = x;
+        for (int i = blockDim.x + threadIdx.x; i < k; i += blockDim.x) picks[i] = kEmpty;
+        __syncthreads();
+    } else if (n2 <= kSortCap) {
         // every live key sits below n2; picks in [n2, k) stay EMPTY
         int fill = n2 > k ? n2 : k;
         for (int i = threadIdx.x; i < fill; i += blockDim.x) sbuf[i] = loader(i);
@@ -284,9 +388,15 @@ __global__ void __launch_bounds__(256) select_fused_kernel(
         block_topk(loader, count, k, sbuf, sbuf, k);  // in-place: out aliases the buffer front
     }
     int width = top_k + window + sink;
-    SmemPicks pk{picks};
-    expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
-               scan_smem);
+    if (k * cap <= kMemberPrefetch) {
+        int* mem = reinterpret_cast<int*>(sbuf + k);
+        expand_row_prefetched(picks, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
+                              lengths + r, scan_smem, mem);
+    } else {
+        SmemPicks pk{picks};
+        expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+                   scan_smem);
+    }
 }
 
 // ------------------------------------------------------------------ host helpers
@@ -434,20 +544,35 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
     int32_t* tickets = counters;
     // columns any row can see: the grid covers the widest row (max_position < 0: all N)
     int64_t most = max_position < 0 ? N : (max_position / block * bpb < N ? max_position / block * bpb : N);
-    int cols = 8;  // one column per warp: the centroid read spreads over many SMs
+    int cols = kFusedThreads / 32;  // one column per warp: the centroid read spreads over many SMs
     int chunks_x = (int)((most + cols - 1) / cols);
     if (chunks_x < 1) chunks_x = 1;
     dim3 grid((unsigned)chunks_x, (unsigned)R);
+    int64_t k = top_p < N ? top_p : N;
+    int64_t staged = k * cap <= kMemberPrefetch ? k * cap : 0;
     int smem = sort_smem_bytes(most);
+    if (smem < kFusedThreads * 8) smem = kFusedThreads * 8;
     if (smem < top_p * 8) smem = (int)(top_p * 8);
+    if (smem < k * 8 + staged * 4) smem = (int)(k * 8 + staged * 4);
     int ch = (int)((d / 8 + 31) / 32);
-#define LSA_FS(TQ, TC, CH)                                                                                            \
-    do {                                                                                                              \
-        auto kern = select_fused_kernel<TQ, TC, CH>;                                                                  \
-        if (set_smem(kern, smem)) return LSA_ERR_CUDA;                                                                \
-        kern<<<grid, 256, smem, stream>>>((const TQ*)queries, ldq, (const TC*)centroids, N, (int)d, positions, block, \
-                                          bpb, cols, (int)top_p, members, (int)cap, (int)window, (int)sink,           \
-                                          (int)top_k, lists, lengths, ws_keys, tickets);                             \
+    cudaLaunchAttribute pdl;
+    pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = grid;
+    lc.blockDim = dim3(kFusedThreads);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = stream;
+    lc.attrs = &pdl;
+    lc.numAttrs = 1;
+#define LSA_FS(TQ, TC, CH)                                                                                       \
+    do {                                                                                                         \
+        auto kern = select_fused_kernel<TQ, TC, CH>;                                                             \
+        if (set_smem(kern, smem)) return LSA_ERR_CUDA;                                                           \
+        if (cudaLaunchKernelEx(&lc, kern, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d, positions,   \
+                               block, bpb, cols, (int)top_p, members, (int)cap, (int)window, (int)sink,          \
+                               (int)top_k, lists, lengths, ws_keys, tickets) != cudaSuccess)                     \
+            return LSA_ERR_CUDA;                                                                                 \
     } while (0)
 #define LSA_FS_CH(TQ, TC)              \
     do {                               \

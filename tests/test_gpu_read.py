@@ -47,7 +47,7 @@ def test_read_gqa_vs_oracle(oracle, lsa, dtype, hq, hkv, D):
     _check(lsa.read_kernel_tiled.sparse_read_auto(tq, tk, tv, ids, ln, D ** -0.5), want, dtype)
 
 
-@pytest.mark.parametrize("splits", [1, 3, 17, 0])
+@pytest.mark.parametrize("splits", [1, 3, 8, 16, 17, 40, 0])
 def test_decode_row_splits_vs_oracle(oracle, lsa, splits):
     """A 2116-id decode row (cfg-2 width) through forced split counts; 0 = automatic."""
     from lsa_b200.read_kernel_tiled import _read
