@@ -8,10 +8,15 @@
 // Three arms, byte-identical by construction (LSA_SELECT_IMPL):
 //   reference    : scores -> pack (listing) -> best-first top-k -> unpack -> expand
 //   fused_unpack : scores -> pack -> best-first top-k -> expand reading the keys
-//   fused        : ONE launch from index queries to read lists: every CTA scores a slice
-//                  of the visible buckets, the last CTA of a row (atomic ticket) sorts the
-//                  row's packed keys and walks the expansion.
+//   fused        : ONE launch from index queries to read lists: the CTAs of a row's
+//                  thread-block cluster score slices of the buckets into the leader CTA's
+//                  shared memory, which orders the packed keys and walks the expansion
+//                  (rows wider than one cluster: the last CTA by atomic ticket does it).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lsa {
 
@@ -268,19 +273,23 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     int64_t ws = pos + 1 - window;
     if (ws < 0) ws = 0;
     const int total = P * cap;
-    // every member load of this thread is issued before any is consumed: one round trip
+    // addresses first, then every member load of this thread in flight together, then the
+    // stores: one memory round trip for the whole staging
     constexpr int kMaxPer = kMemberPrefetch / kFusedThreads;
-    int vals[kMaxPer];
+    const int32_t* src[kMaxPer];
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         int s = threadIdx.x + i * blockDim.x;
-        vals[i] = -1;
+        src[i] = nullptr;
         if (s < total) {
             int p = s / cap, m = s - p * cap;
             int b = key_bucket(picks[p]);
-            if (b >= 0 && b < member_rows) vals[i] = __ldg(members + (int64_t)b * cap + m);
+            if (b >= 0 && b < member_rows) src[i] = members + (int64_t)b * cap + m;
         }
     }
+    int vals[kMaxPer];
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) vals[i] = src[i] ? __ldg(src[i]) : -1;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
         int s = threadIdx.x + i * blockDim.x;
@@ -293,17 +302,38 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     const int spt = (total + blockDim.x - 1) / blockDim.x;
     const int first = threadIdx.x * spt;
     int cnt = 0;
-    for (int i = 0; i < spt; ++i) {
-        int s = first + i;
-        cnt += (s < total && mem[s] >= 0);
+    if (spt % 4 == 0 && first + spt <= total) {  // contiguous 16-byte reads of this thread's slots
+        for (int i = 0; i < spt; i += 4) {
+            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
+            cnt += (v.x >= 0) + (v.y >= 0) + (v.z >= 0) + (v.w >= 0);
+        }
+    } else {
+        for (int i = 0; i < spt; ++i) {
+            int s = first + i;
+            cnt += (s < total && mem[s] >= 0);
+        }
     }
     int filled;
     int at = block_exclusive_scan(cnt, scan_smem, &filled);
-    for (int i = 0; i < spt; ++i) {
-        int s = first + i;
-        if (s < total && mem[s] >= 0) {
-            if (at < top_k) out[at] = mem[s];
-            ++at;
+    if (spt % 4 == 0 && first + spt <= total) {
+        for (int i = 0; i < spt && at < top_k; i += 4) {
+            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
+            const int e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (e[u] >= 0) {
+                    if (at < top_k) out[at] = e[u];
+                    ++at;
+                }
+            }
+        }
+    } else {
+        for (int i = 0; i < spt && at < top_k; ++i) {
+            int s = first + i;
+            if (s < total && mem[s] >= 0) {
+                out[at] = mem[s];
+                ++at;
+            }
         }
     }
     if (filled > top_k) filled = top_k;
@@ -390,6 +420,148 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
         int* mem = reinterpret_cast<int*>(sbuf + k);
+        expand_row_prefetched(picks, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
+                              lengths + r, scan_smem, mem);
+    } else {
+        SmemPicks pk{picks};
+        expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+                   scan_smem);
+    }
+}
+
+// ------------------------------------------------------------------ top-32 by warps
+
+// Descending bitonic sort of 32 keys, one per lane, by shuffles only.
+__device__ __forceinline__ int64_t warp_sort32_desc(int64_t x, int lane) {
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            int64_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+            bool lower = (lane & j) == 0, desc = (lane & k) == 0;
+            x = (lower == desc) ? (x > y ? x : y) : (x < y ? x : y);
+        }
+    }
+    return x;
+}
+
+// Sorts a bitonic 32-sequence descending (half-cleaners of strides 16 .. 1).
+__device__ __forceinline__ int64_t warp_clean32_desc(int64_t x, int lane) {
+#pragma unroll
+    for (int j = 16; j > 0; j >>= 1) {
+        int64_t y = __shfl_xor_sync(0xFFFFFFFFu, x, j);
+        x = (lane & j) == 0 ? (x > y ? x : y) : (x < y ? x : y);
+    }
+    return x;
+}
+
+// The 32 greatest of keys[0, n) (EMPTY-padded), sorted descending, into out[0, 32).
+// Every warp folds its 32-key chunks into one sorted list (merging two sorted lists A, B
+// keeps max(A[i], B[31 - i]), a bitonic sequence holding their top 32), then a merge
+// tree over the warps' lists through shared memory. lists: blockDim.x int64.
+__device__ void block_top32_desc(const int64_t* keys, int n, int64_t* lists, int64_t* out) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int64_t x = warp * 32 + lane < n ? keys[warp * 32 + lane] : kEmpty;
+    x = warp_sort32_desc(x, lane);
+    for (int c = warp + nw; c * 32 < n; c += nw) {
+        int64_t y = c * 32 + lane < n ? keys[c * 32 + lane] : kEmpty;
+        y = warp_sort32_desc(y, lane);
+        y = __shfl_sync(0xFFFFFFFFu, y, 31 - lane);
+        x = warp_clean32_desc(x > y ? x : y, lane);
+    }
+    lists[warp * 32 + lane] = x;
+    __syncthreads();
+    for (int step = 1; step < nw; step <<= 1) {
+        if ((warp % (2 * step)) == 0 && warp + step < nw) {
+            int64_t y = lists[(warp + step) * 32 + 31 - lane];
+            x = warp_clean32_desc(x > y ? x : y, lane);
+            lists[warp * 32 + lane] = x;
+        }
+        __syncthreads();
+    }
+    if (warp == 0) out[lane] = x;
+    __syncthreads();
+}
+
+// ------------------------------------------------------------------ cluster select
+
+constexpr int kMaxColsPerWarp = 4;  // cluster path: up to 16 CTAs x 16 warps x 4 columns
+
+// One launch from index queries to read lists, one thread-block cluster per row: every
+// CTA scores 16 * cpw columns and stores their packed keys straight into the shared
+// memory of the cluster's rank-0 CTA (distributed shared memory: no global round trip,
+// no fence, no ticket), prefetching the scored buckets' member rows into L2 on the way;
+// after one cluster barrier the leader orders the keys (warp sorts + merge tree for
+// top_p <= 32) and walks the expansion. grid = (cluster size, R); block = 512.
+template <typename TQ, typename TC, int CHUNKS>
+__global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
+    const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d,
+    const int32_t* __restrict__ positions, int64_t block, int64_t bpb, int cpw, int top_p,
+    const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
+    int32_t* __restrict__ lengths) {
+    extern __shared__ int64_t sbuf[];
+    __shared__ int64_t slists[kFusedThreads];
+    __shared__ int scan_smem[33];
+    pdl_wait();
+    pdl_trigger();
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int cols_per_cta = nw * cpw;
+    const int64_t c0 = (int64_t)rank * cols_per_cta;
+    // column n's key lands at sbuf[n] of the cluster's rank-0 CTA: every CTA stores its keys
+    // there through distributed shared memory before the one cluster barrier
+    int64_t* lead_keys = cluster.map_shared_rank(sbuf, 0);
+    {
+        int nchunks = d >> 3;
+        float x[CHUNKS][8];
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j) {
+            int ch = lane + 32 * j;
+            if (ch < nchunks) load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+        }
+        float part[kMaxColsPerWarp];
+        const int lines = (cap * 4 + 127) / 128;  // 128-byte lines of one member row
+#pragma unroll
+        for (int i = 0; i < kMaxColsPerWarp; ++i) {  // every column's loads in flight together
+            int64_t n = c0 + warp + nw * i;
+            bool live = i < cpw && n < N;
+            part[i] = live ? lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks) : 0.0f;
+            // the leader reads the picked buckets' member rows next: pull every scored
+            // bucket's row into L2 now
+            if (live && lane < lines)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(members + n * cap + lane * 32));
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxColsPerWarp; ++i) {
+            int64_t n = c0 + warp + nw * i;
+            if (i < cpw && n < N) {
+                float p = butterfly_sum(part[i]);
+                if (lane == 0) lead_keys[n] = pack_key(p, (int32_t)n);
+            }
+        }
+    }
+    cluster.sync();  // every column's key is in the leader's shared memory
+    if (rank != 0) return;
+    const int k = (int)min((int64_t)top_p, N);
+    const int64_t pos = positions[r];
+    int64_t vis = pos / block * bpb;
+    int count = (int)(vis < N ? vis : N);
+    if (count < 0) count = 0;
+    const int n2 = next_pow2(max(count, 1));
+    for (int t = count + threadIdx.x; t < max(n2, k); t += blockDim.x) sbuf[t] = kEmpty;  // unseen columns
+    __syncthreads();
+    int64_t* picks = sbuf;
+    if (k <= 32 && count <= (int)blockDim.x * 4) {
+        block_top32_desc(sbuf, count, slists, slists);
+        if ((int)threadIdx.x < 32) picks[threadIdx.x] = slists[threadIdx.x];  // k <= 32: EMPTY tail past k
+        __syncthreads();
+    } else {
+        bitonic_sort_desc(sbuf, n2);
+    }
+    int width = top_k + window + sink;
+    if (k * cap <= kMemberPrefetch) {
+        int* mem = reinterpret_cast<int*>(sbuf + max(k, 32));
         expand_row_prefetched(picks, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
                               lengths + r, scan_smem, mem);
     } else {
@@ -565,14 +737,52 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
     lc.stream = stream;
     lc.attrs = &pdl;
     lc.numAttrs = 1;
+    // cluster path: the row's columns fit one cluster of <= 16 CTAs (16 warps x <= 4 columns)
+    int cpw = (int)((most + 16 * 16 - 1) / (16 * 16));
+    if (cpw < 1) cpw = 1;
+    int cs = (int)((most + 16 * cpw - 1) / (16 * cpw));
+    if (cs < 1) cs = 1;
+    bool use_cluster = cpw <= kMaxColsPerWarp && cs <= 16;
+    int csmem = sort_smem_bytes(most);
+    if (csmem < (k > 32 ? k : 32) * 8 + staged * 4) csmem = (int)((k > 32 ? k : 32) * 8 + staged * 4);
+    if (csmem < k * 8) csmem = (int)(k * 8);
+    if (csmem < cs * 16 * cpw * 8) csmem = cs * 16 * cpw * 8;  // every scored column's key slot
+    cudaLaunchAttribute cattrs[2];
+    cattrs[0] = pdl;
+    cattrs[1].id = cudaLaunchAttributeClusterDimension;
+    cattrs[1].val.clusterDim.x = (unsigned)cs;
+    cattrs[1].val.clusterDim.y = 1;
+    cattrs[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3((unsigned)cs, (unsigned)R);
+    cc.blockDim = dim3(kFusedThreads);
+    cc.dynamicSmemBytes = csmem;
+    cc.stream = stream;
+    cc.attrs = cattrs;
+    cc.numAttrs = 2;
 #define LSA_FS(TQ, TC, CH)                                                                                       \
     do {                                                                                                         \
-        auto kern = select_fused_kernel<TQ, TC, CH>;                                                             \
-        if (set_smem(kern, smem)) return LSA_ERR_CUDA;                                                           \
-        if (cudaLaunchKernelEx(&lc, kern, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d, positions,   \
-                               block, bpb, cols, (int)top_p, members, (int)cap, (int)window, (int)sink,          \
-                               (int)top_k, lists, lengths, ws_keys, tickets) != cudaSuccess)                     \
-            return LSA_ERR_CUDA;                                                                                 \
+        bool launched = false;                                                                                   \
+        if (use_cluster) {                                                                                       \
+            auto ck = select_cluster_kernel<TQ, TC, CH>;                                                         \
+            if (!set_smem(ck, csmem) &&                                                                          \
+                (cs <= 8 || cudaFuncSetAttribute(ck, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==      \
+                                cudaSuccess) &&                                                                  \
+                cudaLaunchKernelEx(&cc, ck, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d, positions, \
+                                   block, bpb, cpw, (int)top_p, members, (int)cap, (int)window, (int)sink,       \
+                                   (int)top_k, lists, lengths) == cudaSuccess)                                   \
+                launched = true;                                                                                 \
+            else                                                                                                 \
+                cudaGetLastError(); /* a refused cluster launch falls back to the ticket kernel */              \
+        }                                                                                                        \
+        if (!launched) {                                                                                         \
+            auto kern = select_fused_kernel<TQ, TC, CH>;                                                         \
+            if (set_smem(kern, smem)) return LSA_ERR_CUDA;                                                       \
+            if (cudaLaunchKernelEx(&lc, kern, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d,          \
+                                   positions, block, bpb, cols, (int)top_p, members, (int)cap, (int)window,      \
+                                   (int)sink, (int)top_k, lists, lengths, ws_keys, tickets) != cudaSuccess)      \
+                return LSA_ERR_CUDA;                                                                             \
+        }                                                                                                        \
     } while (0)
 #define LSA_FS_CH(TQ, TC)              \
     do {                               \
