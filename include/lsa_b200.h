@@ -122,6 +122,41 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
                      int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                      int64_t max_position, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- prefill (tile rows) */
+
+/* Per-64-query-tile selection of the prefill arm. The reference selects per row only
+ * (pipeline.py:248-316); a tile row scores the fp32 sum of its rows' bf16 index queries,
+ * which ranks buckets like the tile mean.
+ * lsa_tile_queries: tq [tiles, d] fp32 = sum over the tile's rows, in row order, of
+ * bf16(index query) (q_dtype fp32 or bf16). */
+int lsa_tile_queries(const void* index_queries, int q_dtype, int64_t T, int64_t ldq, int64_t d, int64_t tile,
+                     float* out, cudaStream_t stream);
+
+int64_t lsa_tile_select_scratch(int64_t T, int64_t tile, int64_t d, int64_t N);
+
+/* flat_select's composition (scores -> packed keys -> best-first top_p -> expansion,
+ * pipeline.py:248-271) over tile rows: visible = the blocks closed before the tile's first
+ * row (visible_counts, pipeline.py:184-186, at the tile start); the walk keeps the first
+ * top_k members of the picks below the tile's block start, then the sinks
+ * [0, min(sink, block_start)) (window 0). lists [tiles, top_k + sink] int32 (-1 padded),
+ * lengths [tiles]. Counters: tiles int32, zero at rest. block % tile == 0. */
+int lsa_tile_select(const void* index_queries, int q_dtype, int64_t T, int64_t ldq, int64_t tile,
+                    const void* centroids, int c_dtype, int64_t N, int64_t d, int64_t block, int64_t bpb,
+                    const int32_t* members, int64_t cap, int64_t top_p, int64_t sink, int64_t top_k, int32_t* lists,
+                    int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                    cudaStream_t stream);
+
+/* The prefill read (read numerics: src/lsa_rocm_lab/port/read_kernel_tiled.py:41-89): row t
+ * of q [B, T, Hq, 128] attends over its tile's list (tile_lists [B, tiles, ldl], lengths
+ * [B, tiles]; ids outside [0, Tk) skipped) and then, causally, its open block
+ * [t / block * block, t] of k/v [B, Tk, Hkv, 128]. dtype bf16 or fp16; Hq / Hkv in
+ * {4, 8, 16}; tile a multiple of 256 / (Hq / Hkv); block a multiple of tile. out like q.
+ * status: device int32, LSA_ERR_TIMEOUT written there if a bounded device wait expired. */
+int lsa_sparse_prefill(const void* q, const void* k, const void* v, int dtype, const int32_t* tile_lists,
+                       const int32_t* tile_lengths, int64_t ldl, int64_t B, int64_t T, int64_t Tk, int64_t Hq,
+                       int64_t Hkv, int64_t D, int64_t tile, int64_t block, float scale, void* out, int32_t* status,
+                       cudaStream_t stream);
+
 /* ---------------------------------------------------------------- tree */
 
 int lsa_tree_plan(int64_t R, int64_t n_built, const int64_t* level_counts, int64_t beam, int64_t size, int64_t nb,

@@ -56,6 +56,21 @@ __global__ void visible_counts_kernel(const int32_t* positions, int64_t R, int64
     }
 }
 
+// Tile queries of the prefill arm: tq[t, j] = fp32 sum over the tile's rows, in row order,
+// of the bf16-rounded index query element (one thread per column j).
+template <typename T>
+__global__ void tile_queries_kernel(const T* __restrict__ iq, int64_t R, int64_t ldq, int64_t d, int64_t tile,
+                                    float* __restrict__ out) {
+    int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t t = blockIdx.y;
+    if (j >= d) return;
+    int64_t r1 = min((t + 1) * tile, R);
+    float acc = 0.0f;
+    for (int64_t r = t * tile; r < r1; ++r)
+        acc = __fadd_rn(acc, __bfloat162float(__float2bfloat16_rn(to_f32(iq[r * ldq + j]))));
+    out[t * d + j] = acc;
+}
+
 __global__ void pack_keys_kernel(const float* __restrict__ s, int64_t R, int64_t N, int64_t lds,
                                  const int32_t* __restrict__ lengths, int64_t* __restrict__ keys, int64_t ldk) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -233,6 +248,20 @@ struct GlobalKeysCg {
     __device__ int64_t operator()(int i) const { return i < count ? __ldcg(row + i) : kEmpty; }
 };
 
+// Where a selection row stands. Token rows (tile == 0) use positions[r] for both the
+// visible count and the walk. Tile rows (tile > 0, the prefill arm) are the query tiles
+// [r * tile, (r + 1) * tile): the visible count is taken at the tile's first row and the
+// walk runs at the virtual position block_start - 1 with window 0, so a tile's list holds
+// the picked members of closed blocks and the sinks below the tile's open block.
+struct RowPos {
+    const int32_t* positions;
+    int64_t tile, block;
+    __device__ __forceinline__ int64_t count_pos(int r) const { return tile ? r * tile : (int64_t)positions[r]; }
+    __device__ __forceinline__ int64_t walk_pos(int r) const {
+        return tile ? r * tile / block * block - 1 : (int64_t)positions[r];
+    }
+};
+
 constexpr int kFusedThreads = 512;
 constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
 
@@ -358,7 +387,7 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
 template <typename TQ, typename TC, int CHUNKS>
 __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d,
-    const int32_t* __restrict__ positions, int64_t block, int64_t bpb, int cols_per_cta, int top_p,
+    RowPos rp, int64_t block, int64_t bpb, int cols_per_cta, int top_p,
     const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
     int32_t* __restrict__ lengths, int64_t* __restrict__ ws_keys, int32_t* __restrict__ tickets) {
     extern __shared__ int64_t sbuf[];
@@ -394,8 +423,8 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    int64_t pos = positions[r];
-    int64_t vis = pos / block * bpb;
+    int64_t pos = rp.walk_pos(r);
+    int64_t vis = rp.count_pos(r) / block * bpb;
     int count = (int)(vis < N ? vis : N);
     if (count < 0) count = 0;
     int k = (int)min((int64_t)top_p, N);
@@ -496,7 +525,7 @@ constexpr int kMaxColsPerWarp = 4;  // cluster path: up to 16 CTAs x 16 warps x 
 template <typename TQ, typename TC, int CHUNKS>
 __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d,
-    const int32_t* __restrict__ positions, int64_t block, int64_t bpb, int cpw, int top_p,
+    RowPos rp, int64_t block, int64_t bpb, int cpw, int top_p,
     const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
     int32_t* __restrict__ lengths) {
     extern __shared__ int64_t sbuf[];
@@ -544,8 +573,8 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     cluster.sync();  // every column's key is in the leader's shared memory
     if (rank != 0) return;
     const int k = (int)min((int64_t)top_p, N);
-    const int64_t pos = positions[r];
-    int64_t vis = pos / block * bpb;
+    const int64_t pos = rp.walk_pos(r);
+    int64_t vis = rp.count_pos(r) / block * bpb;
     int count = (int)(vis < N ? vis : N);
     if (count < 0) count = 0;
     const int n2 = next_pow2(max(count, 1));
@@ -703,11 +732,14 @@ int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk,
 // per row, zero before the call; the kernel leaves them zero.
 int64_t lsa_select_fused_scratch(int64_t R, int64_t N) { return ((R * N * 8 + 255) / 256) * 256; }
 
-int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
-                     int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
-                     int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
-                     int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
-                     int64_t max_position, cudaStream_t stream) {
+}  // extern "C"
+
+// The fused selection's launch for token rows and tile rows alike (RowPos).
+static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids,
+                               int c_dtype, int64_t N, int64_t d, RowPos positions, int64_t block, int64_t bpb,
+                               const int32_t* members, int64_t cap, int64_t top_p, int64_t window, int64_t sink,
+                               int64_t top_k, int32_t* lists, int32_t* lengths, void* scratch, int64_t scratch_bytes,
+                               int32_t* counters, int64_t n_counters, int64_t max_position, cudaStream_t stream) {
     if (d <= 0 || d % 8 || d > 2048 || ldq % 8 || cap <= 0 || block <= 0) return LSA_ERR_ARG;
     if (!aligned16(queries) || !aligned16(centroids) || !aligned16(scratch)) return LSA_ERR_ARG;
     if (top_p > 4096 || scratch_bytes < lsa_select_fused_scratch(R, N) || n_counters < R) return LSA_ERR_ARG;
@@ -799,6 +831,60 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
 #undef LSA_FS
     LSA_LAUNCH_CHECK();
     return LSA_OK;
+}
+
+extern "C" {
+
+int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                     int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
+                     int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
+                     int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                     int64_t max_position, cudaStream_t stream) {
+    if (positions == nullptr) return LSA_ERR_ARG;
+    return select_fused_launch(queries, q_dtype, R, ldq, centroids, c_dtype, N, d, RowPos{positions, 0, block}, block,
+                               bpb, members, cap, top_p, window, sink, top_k, lists, lengths, scratch, scratch_bytes,
+                               counters, n_counters, max_position, stream);
+}
+
+// ------------------------------------------------------------------ tile rows (prefill)
+
+int lsa_tile_queries(const void* index_queries, int q_dtype, int64_t T, int64_t ldq, int64_t d, int64_t tile,
+                     float* out, cudaStream_t stream) {
+    if (T < 0 || d <= 0 || tile <= 0 || ldq < d || (q_dtype != kF32 && q_dtype != kBF16)) return LSA_ERR_ARG;
+    if (T == 0) return LSA_OK;
+    int64_t tiles = (T + tile - 1) / tile;
+    dim3 grid((unsigned)((d + 255) / 256), (unsigned)tiles);
+    if (q_dtype == kF32)
+        tile_queries_kernel<float><<<grid, 256, 0, stream>>>((const float*)index_queries, T, ldq, d, tile, out);
+    else
+        tile_queries_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const __nv_bfloat16*)index_queries, T, ldq, d,
+                                                                       tile, out);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
+
+int64_t lsa_tile_select_scratch(int64_t T, int64_t tile, int64_t d, int64_t N) {
+    if (tile <= 0) return 0;
+    int64_t tiles = (T + tile - 1) / tile;
+    return ((tiles * d * 4 + 255) / 256) * 256 + lsa_select_fused_scratch(tiles, N);
+}
+
+int lsa_tile_select(const void* index_queries, int q_dtype, int64_t T, int64_t ldq, int64_t tile,
+                    const void* centroids, int c_dtype, int64_t N, int64_t d, int64_t block, int64_t bpb,
+                    const int32_t* members, int64_t cap, int64_t top_p, int64_t sink, int64_t top_k, int32_t* lists,
+                    int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                    cudaStream_t stream) {
+    if (tile <= 0 || T < 0 || block <= 0 || block % tile) return LSA_ERR_ARG;
+    if (scratch_bytes < lsa_tile_select_scratch(T, tile, d, N) || !aligned16(scratch)) return LSA_ERR_ARG;
+    if (T == 0) return LSA_OK;
+    int64_t tiles = (T + tile - 1) / tile;
+    float* tq = (float*)scratch;
+    int64_t tq_bytes = ((tiles * d * 4 + 255) / 256) * 256;
+    int rc = lsa_tile_queries(index_queries, q_dtype, T, ldq, d, tile, tq, stream);
+    if (rc) return rc;
+    return select_fused_launch(tq, kF32, tiles, d, centroids, c_dtype, N, d, RowPos{nullptr, tile, block}, block, bpb,
+                               members, cap, top_p, 0, sink, top_k, lists, lengths, (char*)scratch + tq_bytes,
+                               scratch_bytes - tq_bytes, counters, n_counters, (tiles - 1) * tile, stream);
 }
 
 }  // extern "C"

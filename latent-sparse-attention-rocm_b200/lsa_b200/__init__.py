@@ -7,7 +7,7 @@ errors. Every operator runs hand-written CUDA kernels through the C-ABI library
 ``liblsa_b200.so`` (``include/lsa_b200.h``); there is no CPU path.
 """
 
-from . import _lib, pipeline, read_kernel, read_kernel_tiled, select_fused  # noqa: F401
+from . import _lib, pipeline, prefill, read_kernel, read_kernel_tiled, select_fused  # noqa: F401
 from .index_space import make_index_space  # noqa: F401
 from .pipeline import (  # noqa: F401
     Buckets,

@@ -53,6 +53,11 @@ SIGNATURES = {
     "lsa_pair_to_size_workspace": (_I, [_I, _I, _I]),
     "lsa_pair_to_size": (_INT, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P]),
     "lsa_sparse_read_noalloc": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _I, _P]),
+    "lsa_tile_queries": (_INT, [_P, _INT, _I, _I, _I, _I, _P, _P]),
+    "lsa_tile_select_scratch": (_I, [_I, _I, _I, _I]),
+    "lsa_tile_select": (_INT, [_P, _INT, _I, _I, _I, _P, _INT, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _I,
+                               _P, _I, _P]),
+    "lsa_sparse_prefill": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P]),
     "lsa_tree_plan": (_INT, [_I, _I, _P, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_tree_select": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P,
                                _I, _P]),
@@ -115,6 +120,7 @@ class _Workspace:
     def __init__(self):
         self.scratch: dict = {}
         self.counters: dict = {}
+        self.status: dict = {}
 
 
 _ws = _Workspace()
@@ -132,6 +138,17 @@ def scratch(nbytes: int, device: torch.device) -> torch.Tensor:
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
         _ws.scratch[key] = buf
+    return buf
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """A device int32 status word per (device, stream) that kernels set on a failed
+    bounded wait (LSA_ERR_TIMEOUT); zero while nothing has gone wrong."""
+    key = _key(device)
+    buf = _ws.status.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _ws.status[key] = buf
     return buf
 
 

@@ -224,7 +224,7 @@ void ora_sparse_read(const float *q, const float *k, const float *v, const i32 *
                 i64 n = 0;
                 for (i64 j = 0; j < len; ++j) {
                     i32 id = ids[row * width + j];
-                    if (id < 0) continue;
+                    if (id < 0 || id >= Tk) continue; /* the reference leaves id >= Tk undefined; skipped here */
                     const float *kv = k + ((b * Tk + id) * Hkv + kh) * D;
                     double dot = 0.0;
                     for (i64 e = 0; e < D; ++e) dot += (double)qv[e] * (double)kv[e];
@@ -236,7 +236,7 @@ void ora_sparse_read(const float *q, const float *k, const float *v, const i32 *
                 double l = 0.0;
                 for (i64 j = 0; j < len && n > 0; ++j) {
                     i32 id = ids[row * width + j];
-                    if (id < 0) continue;
+                    if (id < 0 || id >= Tk) continue;
                     double p = exp(s[j] - m);
                     l += p;
                     const float *vv = v + ((b * Tk + id) * Hkv + kh) * D;
