@@ -315,6 +315,87 @@ def run_b200(args, rank, world, dev):
     return result, layers
 
 
+# --------------------------------------------------------------------------- prefill leg
+
+
+def run_prefill(args, dev):
+    """cfg 3: prefill select+read at T tokens (default 32k), bf16, per-64-query-tile top-32.
+
+    Times, on inputs resident in HBM (q 268 MB + K/V 134 MB at 32k, larger than L2, so
+    no flush): the tile selection, the tensor-core prefill read, select+read together, and
+    dense causal SDPA with the cuDNN backend forced. tok/s = T / (select+read time)."""
+    import torch
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    import lsa_b200 as lsa
+    from lsa_b200 import prefill, synthetic
+
+    T = args.prefill_T
+    q, k, v = synthetic.qkv(T, HQ, HKV, DH, SEED + 3, dev)
+    pcfg = lsa.PortConfig(**CFG)
+    iq, ik = lsa.make_index_space(q, k)
+    buckets = lsa.build_buckets_gpu(ik, pcfg)
+    scale = DH ** -0.5
+    stream = torch.cuda.Stream(dev)
+
+    def timed(fn, reps):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                fn()
+            stream.synchronize()
+            ev0.record(stream)
+            for _ in range(reps):
+                fn()
+            ev1.record(stream)
+            stream.synchronize()
+        return ev0.elapsed_time(ev1) / reps
+
+    with torch.cuda.stream(stream):
+        tl, tn = prefill.tile_select(iq, buckets, pcfg)
+        stream.synchronize()
+    reps = max(args.steps, 1)
+    ms_select = timed(lambda: prefill.tile_select(iq, buckets, pcfg), reps)
+    ms_read = timed(lambda: prefill.sparse_prefill(q, k, v, tl, tn, pcfg.cluster_block_size, scale), reps)
+    with ClockSampler(dev.index) as clocks:
+        ms_total = timed(lambda: prefill.lsa_prefill(q, k, v, iq, buckets, pcfg, scale), reps)
+    status = prefill.status(dev)
+    # algorithmic work: every row's keys = its tile's list + its open block [bs, t]
+    rows = torch.arange(T, device=dev)
+    keys_per_row = tn.long()[rows // 64] + (rows % pcfg.cluster_block_size) + 1
+    total_keys = int(keys_per_row.sum().item())
+    flops = 4 * DH * HQ * total_keys
+    dense_flops = 4 * DH * HQ * T * (T + 1) // 2
+    ms_dense = float("nan")
+    if not args.quick:
+        qt, kt, vt = (x.transpose(1, 2) for x in (q, k, v))
+
+        def dense():
+            with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+                return torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=True, scale=scale,
+                                                                        enable_gqa=True)
+
+        ms_dense = timed(dense, max(2, reps // 2))
+    hbm, tflops, peak_kind = _load_peaks()
+    achieved = flops / (ms_read * 1e-3) / 1e12
+    return {
+        "workload": f"prefill{T // 1024}k", "tokens": T, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
+        "tile_queries": 64, "top_p_buckets_per_tile": CFG["top_p"], "budget_tokens": CFG["top_k"],
+        "sink": CFG["sink_size"], "l2": "no flush: q + K/V of one step exceed L2",
+        "tok_per_s": round(T / (ms_total * 1e-3), 1),
+        "ms_select_read": round(ms_total, 4), "ms_select": round(ms_select, 4), "ms_read": round(ms_read, 4),
+        "ms_dense_cudnn": round(ms_dense, 4) if ms_dense == ms_dense else None,
+        "dense_tok_per_s": round(T / (ms_dense * 1e-3), 1) if ms_dense == ms_dense else None,
+        "speedup_vs_dense": round(ms_dense / ms_total, 3) if ms_dense == ms_dense else None,
+        "keys_read": total_keys, "flops": flops, "dense_flops": dense_flops, "status": status,
+        "roofline": {"bound": "tensor", "kernel": "lsa::sparse_prefill_kernel", "achieved": round(achieved, 1),
+                     "peak": tflops, "unit": "TFLOP/s", "frac": round(achieved / tflops, 4), "peak_kind": peak_kind,
+                     "traffic": _traffic_from_profile("sparse_prefill_32k.md")},
+        "clocks": clocks.summary(),
+        "gpu_launches_per_step": 1 + 2 + 1,  # tile queries, fused select (+ its fallback never), read
+    }
+
+
 # --------------------------------------------------------------------------- CPU baseline
 
 
@@ -452,6 +533,8 @@ def main() -> int:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--layers", type=int, default=LAYERS, help="independent 32k caches per step")
     parser.add_argument("--quick", action="store_true", help="skip e2e, dense and CPU legs (profiling runs)")
+    parser.add_argument("--prefill-T", type=int, default=T_CTX, help="prefill leg tokens (0: skip the leg)")
+    parser.add_argument("--only-prefill", action="store_true", help="run the prefill leg alone (profiling runs)")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     LAYERS = args.layers
@@ -473,7 +556,17 @@ def main() -> int:
         import datetime
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.only_prefill:
+        if rank == 0:
+            print(json.dumps(run_prefill(args, dev)), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     result, layers = run_b200(args, rank, world, dev)
+    if args.prefill_T > 0 and rank == 0 and world == 1:
+        del layers[1:]  # free the rotation's caches before the prefill leg
+        torch.cuda.empty_cache()
+        result["prefill"] = run_prefill(args, dev)
     if rank == 0:
         if not args.no_cpu_baseline and not args.quick and world == 1:
             result["cpu_baseline"] = cpu_baseline(layers[0])

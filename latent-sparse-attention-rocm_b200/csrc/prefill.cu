@@ -12,21 +12,31 @@
 // group) pairs, split into two halves of 128 rows (M = 128 each); both halves read the same
 // keys, so every K/V row the CTA gathers feeds 256 rows of tensor-core work. Per chunk of
 // 128 keys of the CTA's list:
-//   S_h  = Q_h K^T     tcgen05.mma kind::f16; Q, K in 128B-swizzled shared memory; S in TMEM
+//   S_h  = Q_h K^T     tcgen05.mma kind::f16, Q and K in 128B-swizzled shared memory, S in TMEM
 //   softmax            one thread per row: S row from TMEM, running max / sum (exp2 domain,
-//                      the O rescale deferred until the max grows by more than 2^8),
-//                      P row (q dtype) into swizzled shared memory
-//   O_h += P_h V       tcgen05.mma with V as an MN-major operand; O in TMEM
-// TMEM columns: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
+//                      the O rescale deferred until the max grows by more than 2^8); P is
+//                      written back over S in TMEM (two 16-bit values per column)
+//   O_h += P_h V       tcgen05.mma with A = P from TMEM and V as an MN-major smem operand
+// TMEM columns: S_0/P_0 [0,128), S_1/P_1 [128,256), O_0 [256,384), O_1 [384,512).
+// Rows reach shared memory by TMA gathers (tile::gather4: four rows by index per copy,
+// 128-byte swizzle applied by the copy engine): Q once, K and V per chunk into 3 + 2 stages.
+// The MMA issue order S_0(j) S_1(j) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... keeps one half's
+// MMAs running while the other half's softmax works; tcgen05 operations of one thread run
+// in order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and O_h is current
+// whenever the softmax sees S_h(j+1).
 // Warp roles (12 warps): warp 0 issues the MMAs (one thread) and owns the TMEM allocation;
-// warp 1 gathers K rows, warp 2 gathers V rows (cp.async, 16 B per lane, zero-fill for
-// skipped ids); warp 3 loads Q; warps 4-7 / 8-11 run the softmax of half 0 / half 1.
-// The S MMA of chunk j+1 is issued before the PV MMA of chunk j, so the tensor core works
-// on one half while the softmax warps work on the other chunk.
+// warp 1 gathers K, warp 2 gathers V, warp 3 gathers Q; warps 4-7 / 8-11 run the softmax
+// of half 0 / half 1.
 //
 // Every wait is bounded (1 s of %globaltimer, warp-uniform); a wait that expires raises a
-// CTA-wide abort flag, every role leaves its loop, the MMA warp drains its MMAs before the
-// TMEM is released, and LSA_ERR_TIMEOUT lands in the status word.
+// CTA-wide abort flag, every role leaves its loop, the MMA warp drains its MMAs and the
+// loaders their copies before the TMEM is released, and LSA_ERR_TIMEOUT lands in the
+// status word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "umma.cuh"
 
@@ -34,28 +44,26 @@ namespace lsa {
 namespace {
 
 constexpr int kPfThreads = 384;
-constexpr int kChunk = 128;                 // keys per step
-constexpr int kTileBytes = 128 * 128 * 2;   // one 128 x 128 16-bit operand tile (two 16 KB blocks)
-constexpr int kBlockBytes = 16384;          // one 64-column block of a tile
-constexpr int kKStages = 2;
-constexpr int kVStages = 1;
+constexpr int kChunk = 128;                // keys per step
+constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 16-bit operand tile (two 16 KB blocks)
+constexpr int kBlockBytes = 16384;         // one 64-column block of a tile
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + 2 * kTileBytes;
 constexpr int kOffV = kOffK + kKStages * kTileBytes;
-constexpr int kOffP = kOffV + kVStages * kTileBytes;
-constexpr int kOffBar = kOffP + 2 * kTileBytes;
+constexpr int kOffBar = kOffV + kVStages * kTileBytes;
 
 enum : int {
     kBarQ = 0,
-    kBarKFull = 1,                         // kKStages
-    kBarKEmpty = kBarKFull + kKStages,     // kKStages
-    kBarVFull = kBarKEmpty + kKStages,     // kVStages
-    kBarVEmpty = kBarVFull + kVStages,     // kVStages
-    kBarSFull = kBarVEmpty + kVStages,     // 2 halves
-    kBarSFree = kBarSFull + 2,             // 2
-    kBarPFull = kBarSFree + 2,             // 2
-    kBarPFree = kBarPFull + 2,             // 2
-    kBarDrain = kBarPFree + 2,
+    kBarKFull = 1,                      // kKStages
+    kBarKEmpty = kBarKFull + kKStages,  // kKStages
+    kBarVFull = kBarKEmpty + kKStages,  // kVStages
+    kBarVEmpty = kBarVFull + kVStages,  // kVStages
+    kBarSFull = kBarVEmpty + kVStages,  // 2 halves
+    kBarPFull = kBarSFull + 2,          // 2
+    kBarODone = kBarPFull + 2,
+    kBarDrain = kBarODone + 1,
     kNumBars = kBarDrain + 1
 };
 
@@ -66,9 +74,6 @@ static_assert(kSmemBytes <= 232448, "prefill shared memory exceeds the per-CTA l
 constexpr uint64_t kWaitNs = 1000000000ull;
 
 struct PrefillArgs {
-    const void* q;
-    const void* k;
-    const void* v;
     const int32_t* lists;    // [B, tiles, ldl]
     const int32_t* lengths;  // [B, tiles]
     void* out;
@@ -105,16 +110,11 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Byte offset of 16-byte chunk c (0..15) of row r in a swizzled 128 x 128 tile.
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-    return (uint32_t)((c >> 3) * kBlockBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
-}
-
 // The softmax warpgroup of one half (warps 4-7: half 0, 8-11: half 1), one thread per row.
 template <typename T, typename KeyId>
-__device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint32_t sbase, uint64_t* bars,
-                                             volatile int* abort_flag, uint32_t tmem, const KeyId& key_id, int64_t t0,
-                                             int64_t bs, int Lt, int nchunks) {
+__device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bars, volatile int* abort_flag,
+                                             uint32_t tmem, const KeyId& key_id, int64_t t0, int64_t bs, int Lt,
+                                             int nchunks) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kvh = blockIdx.x, b = blockIdx.z;
     const int h = (warp - 4) >> 2, qd = warp & 3, r = qd * 32 + lane;
@@ -125,63 +125,70 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint32_t sbas
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     const uint32_t tS = tmem + lane_base + h * 128;
     const uint32_t tO = tmem + lane_base + 256 + h * 128;
-    const uint32_t prow = sbase + kOffP + h * kTileBytes;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nchunks; ++j) {
-        uint32_t vm[4];  // columns of this chunk with a readable key (lane l: column l + 32 m)
+    // ids of the chunk about to be scored (lane l: columns l + 32 m), one chunk ahead
+    int idn[4];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) vm[m] = __ballot_sync(0xFFFFFFFFu, key_id(j * kChunk + lane + 32 * m) >= 0);
+    for (int m = 0; m < 4; ++m) idn[m] = key_id(lane + 32 * m);
+    const float sl = a.scale_log2;
+    const float thresh = 8.0f / sl;  // defer the O rescale until the max grows by 2^8
+    for (int j = 0; j < nchunks; ++j) {
+        uint32_t vm[4];  // columns of this chunk with a readable key
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            vm[m] = __ballot_sync(0xFFFFFFFFu, idn[m] >= 0);
+            idn[m] = key_id((j + 1) * kChunk + lane + 32 * m);
+        }
         ok = warp_wait(&bars[kBarSFull + h], j & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         uint32_t sr[128];
         tmem_ld64_wait<0>(tS, sr);
         tmem_ld64_wait<64>(tS + 64, sr);
-        tc_fence_before();
-        mbar_arrive(&bars[kBarSFree + h]);
         const int cmax = limit - j * kChunk;  // columns <= cmax pass the causal bound
-        float mx = -INFINITY;
+        const bool full = (vm[0] & vm[1] & vm[2] & vm[3]) == 0xFFFFFFFFu && cmax >= kChunk - 1;
+        if (!__all_sync(0xFFFFFFFFu, full)) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-            const bool live = ((vm[c >> 5] >> (c & 31)) & 1u) && c <= cmax;
-            const float x = live ? __uint_as_float(sr[c]) * a.scale_log2 : -INFINITY;
-            sr[c] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
+            for (int c = 0; c < 128; ++c) {
+                const bool live = ((vm[c >> 5] >> (c & 31)) & 1u) && c <= cmax;
+                if (!live) sr[c] = 0xFF800000u;  // -inf
+            }
         }
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
+#pragma unroll
+        for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
+        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float m_new = fmaxf(m_used, mx);
         float alpha = 1.0f;
-        const bool resc = m_new > m_used + 8.0f;
+        const bool resc = m_new > m_used + thresh;
         if (resc) {
-            alpha = exp2f(m_used - m_new);
+            alpha = ex2_approx((m_used - m_new) * sl);
             m_used = m_new;
         }
-        const float ref = m_used == -INFINITY ? 0.0f : m_used;
-        float sum = 0.0f;
+        const float neg = m_used == -INFINITY ? 0.0f : -m_used * sl;
+        float sum8[8];
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-            const float p = exp2f(__uint_as_float(sr[c]) - ref);
-            sr[c] = __float_as_uint(p);
-            sum += p;
-        }
-        l = l * alpha + sum;
-        if (j > 0) {
-            // PV of the previous chunk done: its P buffer is free and O is current
-            ok = warp_wait(&bars[kBarPFree + h], (j - 1) & 1, abort_flag);
-            if (!ok) break;
-            tc_fence_after();
-        }
+        for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
 #pragma unroll
-        for (int c16 = 0; c16 < 16; ++c16) {
-            uint4 w;
-            w.x = pack2(__uint_as_float(sr[8 * c16 + 0]), __uint_as_float(sr[8 * c16 + 1]), (T*)nullptr);
-            w.y = pack2(__uint_as_float(sr[8 * c16 + 2]), __uint_as_float(sr[8 * c16 + 3]), (T*)nullptr);
-            w.z = pack2(__uint_as_float(sr[8 * c16 + 4]), __uint_as_float(sr[8 * c16 + 5]), (T*)nullptr);
-            w.w = pack2(__uint_as_float(sr[8 * c16 + 6]), __uint_as_float(sr[8 * c16 + 7]), (T*)nullptr);
-            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(prow + swz(r, c16)), "r"(w.x),
-                         "r"(w.y), "r"(w.z), "r"(w.w)
-                         : "memory");
+        for (int half = 0; half < 2; ++half) {  // P columns [32 half, 32 half + 32) = keys 64 half ..
+            uint32_t pk[32];
+#pragma unroll
+            for (int c2 = 0; c2 < 32; ++c2) {
+                const int c = 64 * half + 2 * c2;
+                const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sl, neg));
+                const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sl, neg));
+                sum8[c & 7] += p0;
+                sum8[(c + 1) & 7] += p1;
+                pk[c2] = pack2(p0, p1, (T*)nullptr);
+            }
+            tmem_st32(tS + 32 * half, pk);  // P_h over S_h's first 64 columns
         }
+        l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+        // O_h is current here: PV_h(j-1) was issued before S_h(j) and tcgen05 runs in order
         if (j > 0 && __any_sync(0xFFFFFFFFu, resc)) {
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
@@ -191,17 +198,16 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint32_t sbas
                 for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                 tmem_st32(tO + cc * 32, o);
             }
-            tmem_wait_st();
         }
-        fence_proxy_async_smem();
+        tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars[kBarPFull + h]);
     }
-    if (ok && nchunks > 0) ok = warp_wait(&bars[kBarPFree + h], (nchunks - 1) & 1, abort_flag);
+    if (ok && nchunks > 0) ok = warp_wait(&bars[kBarODone], 0, abort_flag);
+    T* orow = static_cast<T*>(a.out) + (((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) * 128;
     if (ok && nchunks > 0) {
         tc_fence_after();
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        T* orow = static_cast<T*>(a.out) + (((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) * 128;
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
             uint32_t o[32];
@@ -218,14 +224,15 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint32_t sbas
                 }
             }
         }
-    } else if (live_row && nchunks == 0) {
-        T* orow = static_cast<T*>(a.out) + (((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) * 128;
+    } else if (ok && live_row) {
         for (int i = 0; i < 16; ++i) reinterpret_cast<uint4*>(orow)[i] = make_uint4(0, 0, 0, 0);
     }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kPfThreads, 1) sparse_prefill_kernel(const PrefillArgs a) {
+__global__ void __launch_bounds__(kPfThreads, 1)
+    sparse_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(sm);
@@ -245,9 +252,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) sparse_prefill_kernel(const Pre
     const int64_t tend = t0 + QC < a.T ? t0 + QC : a.T;
     const int L = Lt + (int)(tend - bs);  // list, then the open block [bs, tend)
     const int nchunks = (L + kChunk - 1) / kChunk;
-    const T* qg = static_cast<const T*>(a.q);
-    const T* kg = static_cast<const T*>(a.k);
-    const T* vg = static_cast<const T*>(a.v);
 
     // key row of list position i (-1: skipped)
     auto key_id = [&](int i) -> int {
@@ -260,21 +264,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) sparse_prefill_kernel(const Pre
     };
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars[kBarQ], 32);
+        mbar_init(&bars[kBarQ], 1);
         for (int s = 0; s < kKStages; ++s) {
-            mbar_init(&bars[kBarKFull + s], 32);
+            mbar_init(&bars[kBarKFull + s], 1);
             mbar_init(&bars[kBarKEmpty + s], 1);
         }
         for (int s = 0; s < kVStages; ++s) {
-            mbar_init(&bars[kBarVFull + s], 32);
+            mbar_init(&bars[kBarVFull + s], 1);
             mbar_init(&bars[kBarVEmpty + s], 1);
         }
         for (int h = 0; h < 2; ++h) {
             mbar_init(&bars[kBarSFull + h], 1);
-            mbar_init(&bars[kBarSFree + h], 128);
             mbar_init(&bars[kBarPFull + h], 128);
-            mbar_init(&bars[kBarPFree + h], 1);
         }
+        mbar_init(&bars[kBarODone], 1);
         mbar_init(&bars[kBarDrain], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -288,112 +291,131 @@ __global__ void __launch_bounds__(kPfThreads, 1) sparse_prefill_kernel(const Pre
     // registers, the two softmax warpgroups take them: 128 x 96 + 256 x 192 <= 384 x 168
     if (warp >= 4) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 192;" ::: "memory");
-        softmax_role<T>(a, sbase, bars, abort_flag, tmem, key_id, t0, bs, Lt, nchunks);
+        softmax_role<T>(a, bars, abort_flag, tmem, key_id, t0, bs, Lt, nchunks);
     } else {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
         if (warp == 0) {
-            // ---------------------------------------------------------------- MMA issue
+            // ------------------------------------------------------------ MMA issue
             constexpr uint32_t idS = umma_idesc_f16<T>(128, 128, false);
             constexpr uint32_t idPV = umma_idesc_f16<T>(128, 128, true);
-            bool ok = warp_wait(&bars[kBarQ], 0, abort_flag);
-            for (int j = 0; ok && j <= nchunks; ++j) {
-                if (j < nchunks) {
-                    const int s = j % kKStages;
-                    ok = warp_wait(&bars[kBarKFull + s], (j / kKStages) & 1, abort_flag);
-                    for (int h = 0; ok && h < 2; ++h) {
-                        if (j > 0) ok = warp_wait(&bars[kBarSFree + h], (j - 1) & 1, abort_flag);
-                        if (!ok) break;
-                        if (lane == 0) {
-                            fence_proxy_async_smem();
-                            tc_fence_after();
-                            const uint32_t qa = sbase + kOffQ + h * kTileBytes, ka = sbase + kOffK + s * kTileBytes;
-#pragma unroll
-                            for (int kk = 0; kk < 8; ++kk) {
-                                const uint32_t off = (kk >> 2) * kBlockBytes + (kk & 3) * 32;
-                                umma_f16_ss(tmem + h * 128, sw128_desc(qa + off, 16, 1024),
-                                            sw128_desc(ka + off, 16, 1024), idS, kk > 0);
-                            }
-                            umma_commit(&bars[kBarSFull + h]);
-                        }
-                        __syncwarp();
+            auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T
+                if (lane == 0) {
+                    const uint32_t qa = sbase + kOffQ + h * kTileBytes;
+                    const uint32_t ka = sbase + kOffK + (j % kKStages) * kTileBytes;
+#pragma unroll 1
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t off = (kk >> 2) * kBlockBytes + (kk & 3) * 32;
+                        umma_f16_ss(tmem + h * 128, sw128_desc(qa + off, 16, 1024), sw128_desc(ka + off, 16, 1024),
+                                    idS, kk > 0);
                     }
-                    if (!ok) break;
-                    if (lane == 0) umma_commit(&bars[kBarKEmpty + s]);
-                    __syncwarp();
+                    umma_commit(&bars[kBarSFull + h]);
                 }
-                if (j > 0) {
-                    const int jj = j - 1, vs = jj % kVStages;
-                    ok = warp_wait(&bars[kBarVFull + vs], (jj / kVStages) & 1, abort_flag);
-                    for (int h = 0; ok && h < 2; ++h) {
-                        ok = warp_wait(&bars[kBarPFull + h], jj & 1, abort_flag);
-                        if (!ok) break;
-                        if (lane == 0) {
-                            fence_proxy_async_smem();
-                            tc_fence_after();
-                            const uint32_t pa = sbase + kOffP + h * kTileBytes, va = sbase + kOffV + vs * kTileBytes;
-#pragma unroll
-                            for (int kk = 0; kk < 8; ++kk) {
-                                const uint32_t aoff = (kk >> 2) * kBlockBytes + (kk & 3) * 32;
-                                umma_f16_ss(tmem + 256 + h * 128, sw128_desc(pa + aoff, 16, 1024),
-                                            sw128_desc(va + kk * 2048, kBlockBytes, 1024), idPV, (jj > 0 || kk > 0));
-                            }
-                            umma_commit(&bars[kBarPFree + h]);
-                        }
-                        __syncwarp();
-                    }
+                __syncwarp();
+            };
+            auto issue_pv = [&](int h, int j) {  // O_h += P_h(j) V_j
+                if (lane == 0) {
+                    const uint32_t va = sbase + kOffV + (j % kVStages) * kTileBytes;
+#pragma unroll 1
+                    for (int kk = 0; kk < 8; ++kk)
+                        umma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8,
+                                    sw128_desc(va + kk * 2048, kBlockBytes, 1024), idPV, (j > 0 || kk > 0));
+                }
+                __syncwarp();
+            };
+            auto commit_to = [&](uint64_t* bar) {
+                if (lane == 0) umma_commit(bar);
+                __syncwarp();
+            };
+            bool ok = warp_wait(&bars[kBarQ], 0, abort_flag);
+            if (ok && nchunks > 0) ok = warp_wait(&bars[kBarKFull], 0, abort_flag);
+            if (ok && nchunks > 0) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                commit_to(&bars[kBarKEmpty]);
+            }
+            for (int j = 0; ok && j < nchunks; ++j) {
+                const bool more = j + 1 < nchunks;
+                ok = warp_wait(&bars[kBarVFull + j % kVStages], (j / kVStages) & 1, abort_flag);
+                if (ok) ok = warp_wait(&bars[kBarPFull + 0], j & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(0, j);
+                if (more) {
+                    const int jn = j + 1;
+                    ok = warp_wait(&bars[kBarKFull + jn % kKStages], (jn / kKStages) & 1, abort_flag);
                     if (!ok) break;
-                    if (lane == 0) umma_commit(&bars[kBarVEmpty + vs]);
-                    __syncwarp();
+                    issue_s(0, jn);
+                }
+                ok = warp_wait(&bars[kBarPFull + 1], j & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(1, j);
+                commit_to(&bars[kBarVEmpty + j % kVStages]);
+                if (more) {
+                    issue_s(1, j + 1);
+                    commit_to(&bars[kBarKEmpty + (j + 1) % kKStages]);
                 }
             }
+            if (ok && nchunks > 0) commit_to(&bars[kBarODone]);
             // every MMA issued so far completes before the TMEM is released
-            if (lane == 0) umma_commit(&bars[kBarDrain]);
-            __syncwarp();
+            commit_to(&bars[kBarDrain]);
             mbar_wait_bounded(&bars[kBarDrain], 0);
             __syncwarp();
         } else if (warp == 1 || warp == 2) {
-            // ---------------------------------------------------------------- K / V gathers
+            // ------------------------------------------------------------ K / V gathers
             const bool isK = warp == 1;
-            const T* src = isK ? kg : vg;
+            const void* map = isK ? (const void*)&kmap : (const void*)&vmap;
             const int stages = isK ? kKStages : kVStages;
             uint64_t* full = &bars[isK ? kBarKFull : kBarVFull];
             uint64_t* empty = &bars[isK ? kBarKEmpty : kBarVEmpty];
             const uint32_t base = sbase + (isK ? kOffK : kOffV);
-            const int64_t row_stride = (int64_t)a.Hkv * 128;
-            const T* src0 = src + ((int64_t)b * a.Tk * a.Hkv + kvh) * 128 + (lane & 15) * 8;
+            const int col0 = kvh * 128;
+            const int brow = (int)((int64_t)b * a.Tk);
+            int issued = 0;
             for (int j = 0; j < nchunks; ++j) {
                 const int s = j % stages;
                 if (j >= stages && !warp_wait(&empty[s], (j / stages - 1) & 1, abort_flag)) break;
-                const int i0 = j * kChunk + lane;
-                const int id0 = key_id(i0), id1 = key_id(i0 + 32), id2 = key_id(i0 + 64), id3 = key_id(i0 + 96);
-                const uint32_t dst0 = base + s * kTileBytes;
-#pragma unroll 1
-                for (int m = 0; m < 4; ++m) {
-                    const int idm = m == 0 ? id0 : (m == 1 ? id1 : (m == 2 ? id2 : id3));
-#pragma unroll 4
-                    for (int i = 0; i < 16; ++i) {
-                        const int row = 32 * m + 2 * i + (lane >> 4);
-                        const int kid = __shfl_sync(0xFFFFFFFFu, idm, row & 31);
-                        const T* g = src0 + (int64_t)(kid < 0 ? 0 : kid) * row_stride;
-                        cp_async16(dst0 + swz(row, lane & 15), g, kid < 0 ? 0u : 16u);
-                    }
+                // lane l gathers rows 4l .. 4l+3 of the chunk; skipped ids read row 0 (masked)
+                int rid[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int id = key_id(j * kChunk + 4 * lane + i);
+                    rid[i] = brow + (id < 0 ? 0 : id);
                 }
-                cp_async_arrive_noinc(&full[s]);
+                if (lane == 0) mbar_arrive_expect_tx(&full[s], kTileBytes);
+                __syncwarp();
+                const uint32_t dst = base + s * kTileBytes + 4 * lane * 128;
+                tma_gather4(dst, map, col0, rid[0], rid[1], rid[2], rid[3], &full[s]);
+                tma_gather4(dst + kBlockBytes, map, col0 + 64, rid[0], rid[1], rid[2], rid[3], &full[s]);
+                issued = j + 1;
             }
-            cp_async_wait_all();
-        } else if (warp == 3) {
-            // ---------------------------------------------------------------- Q tile
-#pragma unroll 2
-            for (int it = 0; it < 128; ++it) {  // 256 rows x 16 chunks over 32 lanes
-                const int lin = it * 32 + lane, row2 = lin >> 4, c = lin & 15;
-                const int h = row2 >> 7, r = row2 & 127, g = r / a.QH, qi = r % a.QH;
-                const int64_t t = t0 + h * a.QH + qi;
-                const bool live = t < a.T;
-                const T* src = qg + (((int64_t)b * a.T + (live ? t : 0)) * a.Hq + (int64_t)kvh * a.G + g) * 128 + c * 8;
-                cp_async16(sbase + kOffQ + h * kTileBytes + swz(r, c), src, live ? 16u : 0u);
+            // the copies in flight land before the CTA leaves: the last fill of each stage
+            for (int j = issued - stages < 0 ? 0 : issued - stages; j < issued; ++j)
+                mbar_wait_bounded(&full[j % stages], (j / stages) & 1);
+            __syncwarp();
+        } else {
+            // ------------------------------------------------------------ Q tile
+            // 256 rows (2 halves x 128) in 64 gathers of 4 rows x 2 column blocks
+            if (lane == 0) mbar_arrive_expect_tx(&bars[kBarQ], 2 * kTileBytes);
+            __syncwarp();
+#pragma unroll
+            for (int k2 = 0; k2 < 2; ++k2) {
+                const int grp = lane * 2 + k2;  // rows 4 grp .. 4 grp + 3 of the 256
+                int rid[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int row2 = 4 * grp + i, h = row2 >> 7, r = row2 & 127, g = r / a.QH, qi = r % a.QH;
+                    const int64_t t = t0 + h * a.QH + qi;
+                    rid[i] = t < a.T ? (int)(((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) : 0;
+                }
+                const int h = (4 * grp) >> 7, r = (4 * grp) & 127;
+                const uint32_t dst = sbase + kOffQ + h * kTileBytes + r * 128;
+                tma_gather4(dst, &qmap, 0, rid[0], rid[1], rid[2], rid[3], &bars[kBarQ]);
+                tma_gather4(dst + kBlockBytes, &qmap, 64, rid[0], rid[1], rid[2], rid[3], &bars[kBarQ]);
             }
-            cp_async_arrive_noinc(&bars[kBarQ]);
-            cp_async_wait_all();
+            mbar_wait_bounded(&bars[kBarQ], 0);
+            __syncwarp();
         }
     }
 
@@ -406,14 +428,49 @@ __global__ void __launch_bounds__(kPfThreads, 1) sparse_prefill_kernel(const Pre
     if (threadIdx.x == 0 && *abort_flag) atomicExch(a.status, LSA_ERR_TIMEOUT);
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D row-gather map over [rows, cols] 16-bit elements: box = 64 columns x 1 row, 128B swizzle.
+bool make_row_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, bool bf16) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <typename T>
-int launch_prefill(const PrefillArgs& a, int64_t B, cudaStream_t stream) {
+int launch_prefill(const void* q, const void* k, const void* v, const PrefillArgs& a, int64_t B,
+                   cudaStream_t stream) {
+    const bool bf16 = UmmaFormat<T>::value == 1;
+    CUtensorMap qm, km, vm;
+    if (!make_row_map(&qm, q, (uint64_t)(B * a.T * a.Hq), 128, bf16) ||
+        !make_row_map(&km, k, (uint64_t)(B * a.Tk), (uint64_t)a.Hkv * 128, bf16) ||
+        !make_row_map(&vm, v, (uint64_t)(B * a.Tk), (uint64_t)a.Hkv * 128, bf16))
+        return LSA_ERR_CUDA;
     auto kern = sparse_prefill_kernel<T>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return LSA_ERR_CUDA;
     const int QC = 2 * a.QH;
     dim3 grid((unsigned)a.Hkv, (unsigned)((a.T + QC - 1) / QC), (unsigned)B);
-    kern<<<grid, kPfThreads, kSmemBytes, stream>>>(a);
+    kern<<<grid, kPfThreads, kSmemBytes, stream>>>(qm, km, vm, a);
     LSA_LAUNCH_CHECK();
     return LSA_OK;
 }
@@ -435,14 +492,12 @@ int lsa_sparse_prefill(const void* q, const void* k, const void* v, int dtype, c
     if (G != 4 && G != 8 && G != 16) return LSA_ERR_ARG;
     const int64_t QH = 128 / G;
     if (tile % (2 * QH) || block % tile) return LSA_ERR_ARG;
-    if (Tk > INT32_MAX || T > INT32_MAX || status == nullptr) return LSA_ERR_ARG;
+    // TMA row coordinates are 32-bit: every gathered row index must fit
+    if (status == nullptr || B * Tk > INT32_MAX || B * T * Hq > INT32_MAX) return LSA_ERR_ARG;
     auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
     if (!al16(q) || !al16(k) || !al16(v) || !al16(out)) return LSA_ERR_ARG;
     if (B == 0 || T == 0) return LSA_OK;
     PrefillArgs a;
-    a.q = q;
-    a.k = k;
-    a.v = v;
     a.lists = tile_lists;
     a.lengths = tile_lengths;
     a.out = out;
@@ -458,8 +513,8 @@ int lsa_sparse_prefill(const void* q, const void* k, const void* v, int dtype, c
     a.block = (int)block;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
-    if (dtype == kBF16) return launch_prefill<__nv_bfloat16>(a, B, stream);
-    if (dtype == kF16) return launch_prefill<__half>(a, B, stream);
+    if (dtype == kBF16) return launch_prefill<__nv_bfloat16>(q, k, v, a, B, stream);
+    if (dtype == kF16) return launch_prefill<__half>(q, k, v, a, B, stream);
     return LSA_ERR_ARG;
 }
 

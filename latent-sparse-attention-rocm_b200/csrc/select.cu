@@ -748,7 +748,11 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     int32_t* tickets = counters;
     // columns any row can see: the grid covers the widest row (max_position < 0: all N)
     int64_t most = max_position < 0 ? N : (max_position / block * bpb < N ? max_position / block * bpb : N);
-    int cols = kFusedThreads / 32;  // one column per warp: the centroid read spreads over many SMs
+    // few rows (decode): one column per warp, the centroid read spread over many SMs;
+    // many rows (prefill tiles): one CTA per row scores all its columns (no cross-CTA merge)
+    const bool many_rows = R >= 64;
+    int cols = kFusedThreads / 32;
+    if (many_rows) cols = (int)(((most > 0 ? most : 1) + 15) / 16 * 16);
     int chunks_x = (int)((most + cols - 1) / cols);
     if (chunks_x < 1) chunks_x = 1;
     dim3 grid((unsigned)chunks_x, (unsigned)R);
@@ -774,7 +778,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     if (cpw < 1) cpw = 1;
     int cs = (int)((most + 16 * cpw - 1) / (16 * cpw));
     if (cs < 1) cs = 1;
-    bool use_cluster = cpw <= kMaxColsPerWarp && cs <= 16;
+    bool use_cluster = !many_rows && cpw <= kMaxColsPerWarp && cs <= 16;
     int csmem = sort_smem_bytes(most);
     if (csmem < (k > 32 ? k : 32) * 8 + staged * 4) csmem = (int)((k > 32 ? k : 32) * 8 + staged * 4);
     if (csmem < k * 8) csmem = (int)(k * 8);
