@@ -18,32 +18,29 @@
 //                      written back over S in TMEM (two 16-bit values per column)
 //   O_h += P_h V       tcgen05.mma with A = P from TMEM and V as an MN-major smem operand
 // TMEM columns: S_0/P_0 [0,128), S_1/P_1 [128,256), O_0 [256,384), O_1 [384,512).
-// Rows reach shared memory by TMA gathers (tile::gather4: four rows by index per copy,
-// 128-byte swizzle applied by the copy engine): Q once, K and V per chunk into 3 + 2 stages.
+// Rows reach shared memory by cp.async from seven loader warps (16 B per copy into the
+// 128B-swizzled layout): Q once, K and V per chunk into 3 + 2 stages. Many small copies in
+// flight beat TMA row gathers here: a tile::gather4 moves 512 B and the copy engine takes
+// roughly 75 cycles per gather, about 7 B/clk per SM.
 // The MMA issue order S_0(j) S_1(j) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... keeps one half's
 // MMAs running while the other half's softmax works; tcgen05 operations of one thread run
 // in order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and O_h is current
 // whenever the softmax sees S_h(j+1).
-// Warp roles (12 warps): warp 0 issues the MMAs (one thread) and owns the TMEM allocation;
-// warp 1 gathers K, warp 2 gathers V, warp 3 gathers Q; warps 4-7 / 8-11 run the softmax
-// of half 0 / half 1.
+// Warp roles (16 warps): warp 0 issues the MMAs (one thread) and owns the TMEM allocation;
+// warps 1-3 and 12-15 load Q, K and V; warps 4-7 / 8-11 run the softmax of half 0 / half 1.
 //
 // Every wait is bounded (1 s of %globaltimer, warp-uniform); a wait that expires raises a
 // CTA-wide abort flag, every role leaves its loop, the MMA warp drains its MMAs and the
 // loaders their copies before the TMEM is released, and LSA_ERR_TIMEOUT lands in the
 // status word.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "common.cuh"
 #include "umma.cuh"
 
 namespace lsa {
 namespace {
 
-constexpr int kPfThreads = 384;
+constexpr int kPfThreads = 512;
+constexpr int kLoaders = 224;  // warps 1-3 and 12-15
 constexpr int kChunk = 128;                // keys per step
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 16-bit operand tile (two 16 KB blocks)
 constexpr int kBlockBytes = 16384;         // one 64-column block of a tile
@@ -74,6 +71,9 @@ static_assert(kSmemBytes <= 232448, "prefill shared memory exceeds the per-CTA l
 constexpr uint64_t kWaitNs = 1000000000ull;
 
 struct PrefillArgs {
+    const void* q;
+    const void* k;
+    const void* v;
     const int32_t* lists;    // [B, tiles, ldl]
     const int32_t* lengths;  // [B, tiles]
     void* out;
@@ -108,6 +108,11 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16*) {
 __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Byte offset of 16-byte chunk c (0..15) of row r in a 128B-swizzled 128 x 128 tile.
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+    return (uint32_t)((c >> 3) * kBlockBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
 // The softmax warpgroup of one half (warps 4-7: half 0, 8-11: half 1), one thread per row.
@@ -231,8 +236,7 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bar
 
 template <typename T>
 __global__ void __launch_bounds__(kPfThreads, 1)
-    sparse_prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                          const __grid_constant__ CUtensorMap vmap, const PrefillArgs a) {
+    sparse_prefill_kernel(const PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(sm);
@@ -264,13 +268,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     };
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars[kBarQ], 1);
+        mbar_init(&bars[kBarQ], kLoaders);
         for (int s = 0; s < kKStages; ++s) {
-            mbar_init(&bars[kBarKFull + s], 1);
+            mbar_init(&bars[kBarKFull + s], kLoaders);
             mbar_init(&bars[kBarKEmpty + s], 1);
         }
         for (int s = 0; s < kVStages; ++s) {
-            mbar_init(&bars[kBarVFull + s], 1);
+            mbar_init(&bars[kBarVFull + s], kLoaders);
             mbar_init(&bars[kBarVEmpty + s], 1);
         }
         for (int h = 0; h < 2; ++h) {
@@ -287,19 +291,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // register split (launch: 384 threads x 168): the loader/MMA warpgroup gives up
-    // registers, the two softmax warpgroups take them: 128 x 96 + 256 x 192 <= 384 x 168
-    if (warp >= 4) {
+    // register split (launch: 512 threads x 128): the MMA/loader warpgroups (0 and 3) give
+    // up registers, the two softmax warpgroups take them: 256 x 64 + 256 x 192 = 512 x 128
+    if (warp >= 4 && warp < 12) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 192;" ::: "memory");
         softmax_role<T>(a, bars, abort_flag, tmem, key_id, t0, bs, Lt, nchunks);
     } else {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
         if (warp == 0) {
             // ------------------------------------------------------------ MMA issue
             constexpr uint32_t idS = umma_idesc_f16<T>(128, 128, false);
             constexpr uint32_t idPV = umma_idesc_f16<T>(128, 128, true);
             auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T
                 if (lane == 0) {
+                    fence_proxy_async_smem();  // cp.async (generic proxy) data -> MMA (async proxy)
                     const uint32_t qa = sbase + kOffQ + h * kTileBytes;
                     const uint32_t ka = sbase + kOffK + (j % kKStages) * kTileBytes;
 #pragma unroll 1
@@ -314,6 +319,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             };
             auto issue_pv = [&](int h, int j) {  // O_h += P_h(j) V_j
                 if (lane == 0) {
+                    fence_proxy_async_smem();
                     const uint32_t va = sbase + kOffV + (j % kVStages) * kTileBytes;
 #pragma unroll 1
                     for (int kk = 0; kk < 8; ++kk)
@@ -362,59 +368,57 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             commit_to(&bars[kBarDrain]);
             mbar_wait_bounded(&bars[kBarDrain], 0);
             __syncwarp();
-        } else if (warp == 1 || warp == 2) {
-            // ------------------------------------------------------------ K / V gathers
-            const bool isK = warp == 1;
-            const void* map = isK ? (const void*)&kmap : (const void*)&vmap;
-            const int stages = isK ? kKStages : kVStages;
-            uint64_t* full = &bars[isK ? kBarKFull : kBarVFull];
-            uint64_t* empty = &bars[isK ? kBarKEmpty : kBarVEmpty];
-            const uint32_t base = sbase + (isK ? kOffK : kOffV);
-            const int col0 = kvh * 128;
-            const int brow = (int)((int64_t)b * a.Tk);
-            int issued = 0;
-            for (int j = 0; j < nchunks; ++j) {
-                const int s = j % stages;
-                if (j >= stages && !warp_wait(&empty[s], (j / stages - 1) & 1, abort_flag)) break;
-                // lane l gathers rows 4l .. 4l+3 of the chunk; skipped ids read row 0 (masked)
-                int rid[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int id = key_id(j * kChunk + 4 * lane + i);
-                    rid[i] = brow + (id < 0 ? 0 : id);
-                }
-                if (lane == 0) mbar_arrive_expect_tx(&full[s], kTileBytes);
-                __syncwarp();
-                const uint32_t dst = base + s * kTileBytes + 4 * lane * 128;
-                tma_gather4(dst, map, col0, rid[0], rid[1], rid[2], rid[3], &full[s]);
-                tma_gather4(dst + kBlockBytes, map, col0 + 64, rid[0], rid[1], rid[2], rid[3], &full[s]);
-                issued = j + 1;
-            }
-            // the copies in flight land before the CTA leaves: the last fill of each stage
-            for (int j = issued - stages < 0 ? 0 : issued - stages; j < issued; ++j)
-                mbar_wait_bounded(&full[j % stages], (j / stages) & 1);
-            __syncwarp();
         } else {
-            // ------------------------------------------------------------ Q tile
-            // 256 rows (2 halves x 128) in 64 gathers of 4 rows x 2 column blocks
-            if (lane == 0) mbar_arrive_expect_tx(&bars[kBarQ], 2 * kTileBytes);
-            __syncwarp();
-#pragma unroll
-            for (int k2 = 0; k2 < 2; ++k2) {
-                const int grp = lane * 2 + k2;  // rows 4 grp .. 4 grp + 3 of the 256
-                int rid[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const int row2 = 4 * grp + i, h = row2 >> 7, r = row2 & 127, g = r / a.QH, qi = r % a.QH;
-                    const int64_t t = t0 + h * a.QH + qi;
-                    rid[i] = t < a.T ? (int)(((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) : 0;
-                }
-                const int h = (4 * grp) >> 7, r = (4 * grp) & 127;
-                const uint32_t dst = sbase + kOffQ + h * kTileBytes + r * 128;
-                tma_gather4(dst, &qmap, 0, rid[0], rid[1], rid[2], rid[3], &bars[kBarQ]);
-                tma_gather4(dst + kBlockBytes, &qmap, 64, rid[0], rid[1], rid[2], rid[3], &bars[kBarQ]);
+            // ------------------------------------------------------------ loads (warps 1-3, 12-15)
+            // 224 threads, 16 B per cp.async, 128B-swizzled destinations: Q once, then K_j and
+            // V_j per chunk into their stages (skipped ids zero-fill their rows: masked anyway)
+            const int lt = (warp < 4 ? warp - 1 : warp - 9) * 32 + lane;
+            const T* qg = static_cast<const T*>(a.q);
+            for (int lin = lt; lin < 4096; lin += kLoaders) {  // 256 rows x 16 chunks
+                const int row2 = lin >> 4, c = lin & 15, h = row2 >> 7, r = row2 & 127, g = r / a.QH, qi = r % a.QH;
+                const int64_t t = t0 + h * a.QH + qi;
+                const bool live = t < a.T;
+                const T* src = qg + (((int64_t)b * a.T + (live ? t : 0)) * a.Hq + (int64_t)kvh * a.G + g) * 128 + c * 8;
+                cp_async16(sbase + kOffQ + h * kTileBytes + swz(r, c), src, live ? 16u : 0u);
             }
-            mbar_wait_bounded(&bars[kBarQ], 0);
+            cp_async_arrive_noinc(&bars[kBarQ]);
+            const int64_t row_stride = (int64_t)a.Hkv * 128;
+            const T* k0 = static_cast<const T*>(a.k) + ((int64_t)b * a.Tk * a.Hkv + kvh) * 128;
+            const T* v0 = static_cast<const T*>(a.v) + ((int64_t)b * a.Tk * a.Hkv + kvh) * 128;
+            // copy `it` of a thread: 16-byte chunk (lt + 224 it) & 15 of row (lt + 224 it) >> 4; the
+            // rows' ids (shared by K_j and V_j) load into registers before the stage waits
+            constexpr int kCopies = (2048 + kLoaders - 1) / kLoaders;
+            int idr[kCopies];
+            auto load_ids = [&](int j) {
+#pragma unroll
+                for (int it = 0; it < kCopies; ++it) {
+                    const int lin = lt + kLoaders * it;
+                    idr[it] = lin < 2048 ? key_id(j * kChunk + (lin >> 4)) : -1;
+                }
+            };
+            auto issue = [&](uint32_t dst, const T* src0) {
+#pragma unroll
+                for (int it = 0; it < kCopies; ++it) {
+                    const int lin = lt + kLoaders * it;
+                    if (lin < 2048) {
+                        const int row = lin >> 4, c = lin & 15, id = idr[it];
+                        cp_async16(dst + swz(row, c), src0 + (int64_t)(id < 0 ? 0 : id) * row_stride + c * 8,
+                                   id < 0 ? 0u : 16u);
+                    }
+                }
+            };
+            if (nchunks > 0) load_ids(0);
+            for (int j = 0; j < nchunks; ++j) {
+                const int sk = j % kKStages, sv = j % kVStages;
+                if (j >= kKStages && !warp_wait(&bars[kBarKEmpty + sk], (j / kKStages - 1) & 1, abort_flag)) break;
+                issue(sbase + kOffK + sk * kTileBytes, k0);
+                cp_async_arrive_noinc(&bars[kBarKFull + sk]);
+                if (j >= kVStages && !warp_wait(&bars[kBarVEmpty + sv], (j / kVStages - 1) & 1, abort_flag)) break;
+                issue(sbase + kOffV + sv * kTileBytes, v0);
+                cp_async_arrive_noinc(&bars[kBarVFull + sv]);
+                if (j + 1 < nchunks) load_ids(j + 1);
+            }
+            cp_async_wait_all();
             __syncwarp();
         }
     }
@@ -428,49 +432,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (threadIdx.x == 0 && *abort_flag) atomicExch(a.status, LSA_ERR_TIMEOUT);
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// 2-D row-gather map over [rows, cols] 16-bit elements: box = 64 columns x 1 row, 128B swizzle.
-bool make_row_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, bool bf16) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {64, 1};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T>
-int launch_prefill(const void* q, const void* k, const void* v, const PrefillArgs& a, int64_t B,
-                   cudaStream_t stream) {
-    const bool bf16 = UmmaFormat<T>::value == 1;
-    CUtensorMap qm, km, vm;
-    if (!make_row_map(&qm, q, (uint64_t)(B * a.T * a.Hq), 128, bf16) ||
-        !make_row_map(&km, k, (uint64_t)(B * a.Tk), (uint64_t)a.Hkv * 128, bf16) ||
-        !make_row_map(&vm, v, (uint64_t)(B * a.Tk), (uint64_t)a.Hkv * 128, bf16))
-        return LSA_ERR_CUDA;
+int launch_prefill(const PrefillArgs& a, int64_t B, cudaStream_t stream) {
     auto kern = sparse_prefill_kernel<T>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return LSA_ERR_CUDA;
     const int QC = 2 * a.QH;
     dim3 grid((unsigned)a.Hkv, (unsigned)((a.T + QC - 1) / QC), (unsigned)B);
-    kern<<<grid, kPfThreads, kSmemBytes, stream>>>(qm, km, vm, a);
+    kern<<<grid, kPfThreads, kSmemBytes, stream>>>(a);
     LSA_LAUNCH_CHECK();
     return LSA_OK;
 }
@@ -492,12 +461,14 @@ int lsa_sparse_prefill(const void* q, const void* k, const void* v, int dtype, c
     if (G != 4 && G != 8 && G != 16) return LSA_ERR_ARG;
     const int64_t QH = 128 / G;
     if (tile % (2 * QH) || block % tile) return LSA_ERR_ARG;
-    // TMA row coordinates are 32-bit: every gathered row index must fit
-    if (status == nullptr || B * Tk > INT32_MAX || B * T * Hq > INT32_MAX) return LSA_ERR_ARG;
+    if (status == nullptr || Tk > INT32_MAX) return LSA_ERR_ARG;
     auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
     if (!al16(q) || !al16(k) || !al16(v) || !al16(out)) return LSA_ERR_ARG;
     if (B == 0 || T == 0) return LSA_OK;
     PrefillArgs a;
+    a.q = q;
+    a.k = k;
+    a.v = v;
     a.lists = tile_lists;
     a.lengths = tile_lengths;
     a.out = out;
@@ -513,8 +484,8 @@ int lsa_sparse_prefill(const void* q, const void* k, const void* v, int dtype, c
     a.block = (int)block;
     a.scale_log2 = scale * 1.4426950408889634f;
     a.status = status;
-    if (dtype == kBF16) return launch_prefill<__nv_bfloat16>(q, k, v, a, B, stream);
-    if (dtype == kF16) return launch_prefill<__half>(q, k, v, a, B, stream);
+    if (dtype == kBF16) return launch_prefill<__nv_bfloat16>(a, B, stream);
+    if (dtype == kF16) return launch_prefill<__half>(a, B, stream);
     return LSA_ERR_ARG;
 }
 
