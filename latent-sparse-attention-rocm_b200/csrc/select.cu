@@ -66,7 +66,8 @@ __global__ void tile_queries_kernel(const T* __restrict__ iq, int64_t R, int64_t
     if (j >= d) return;
     int64_t r1 = min((t + 1) * tile, R);
     float acc = 0.0f;
-    for (int64_t r = t * tile; r < r1; ++r)
+#pragma unroll 16
+    for (int64_t r = t * tile; r < r1; ++r)  // loads run ahead; the adds stay in row order
         acc = __fadd_rn(acc, __bfloat162float(__float2bfloat16_rn(to_f32(iq[r * ldq + j]))));
     out[t * d + j] = acc;
 }
@@ -408,9 +409,25 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
             int ch = lane + 32 * j;
             if (ch < nchunks) load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
         }
-        for (int64_t n = c0 + warp; n < c1; n += blockDim.x >> 5) {
-            float p = butterfly_sum(lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks));
-            if (lane == 0) ws_keys[r * N + n] = pack_key(p, (int32_t)n);
+        // four columns per warp per pass, their centroid loads in flight together; each row
+        // starts at its own column offset so concurrent rows do not all read the same lines
+        const int nw = blockDim.x >> 5;
+        const int64_t span = c1 - c0, rot = ((int64_t)r * 97) % span;
+        for (int64_t i0 = warp; i0 < span; i0 += 4 * nw) {
+            float part[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t ii = i0 + (int64_t)i * nw;
+                const int64_t n = c0 + (ii + rot < span ? ii + rot : ii + rot - span);
+                part[i] = ii < span ? lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks) : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t ii = i0 + (int64_t)i * nw;
+                const int64_t n = c0 + (ii + rot < span ? ii + rot : ii + rot - span);
+                const float p = butterfly_sum(part[i]);
+                if (ii < span && lane == 0) ws_keys[r * N + n] = pack_key(p, (int32_t)n);
+            }
         }
     }
     __threadfence();
