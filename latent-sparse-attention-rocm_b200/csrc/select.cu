@@ -379,6 +379,8 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     if (threadIdx.x == 0) *length_out = filled + nwin + nsink;
 }
 
+__device__ void block_top32_desc(const int64_t* keys, int n, int64_t* lists, int64_t* out);
+
 // One launch from index queries to read lists. grid = (chunks, R), block = 512: every
 // warp scores one visible column; the last CTA of a row (atomic ticket) orders the row's
 // packed keys (register bitonic up to 512 keys) and walks the expansion.
@@ -392,6 +394,7 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
     int32_t* __restrict__ lengths, int64_t* __restrict__ ws_keys, int32_t* __restrict__ tickets) {
     extern __shared__ int64_t sbuf[];
+    __shared__ int64_t slists[kFusedThreads];
     __shared__ int scan_smem[33];
     __shared__ int is_last;
     pdl_wait();
@@ -448,7 +451,14 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     GlobalKeysCg loader{ws_keys + r * N, count};
     int n2 = next_pow2(max(count, 1));
     int64_t* picks = sbuf;  // sorted keys live at the front of the buffer
-    if (count <= (int)blockDim.x) {
+    if (k <= 32 && count <= 4 * (int)blockDim.x) {
+        // top-32: warp sorts + merge tree over the keys staged in shared memory
+        for (int i = threadIdx.x; i < count; i += blockDim.x) sbuf[i] = loader(i);
+        __syncthreads();
+        block_top32_desc(sbuf, count, slists, slists);
+        if ((int)threadIdx.x < 32) picks[threadIdx.x] = slists[threadIdx.x];
+        __syncthreads();
+    } else if (count <= (int)blockDim.x) {
         int64_t x = block_bitonic_desc_regs(loader((int)threadIdx.x), sbuf);
         __syncthreads();  // the exchange buffer becomes the picks
         if ((int)threadIdx.x < k) picks[threadIdx.x] = x;
