@@ -396,6 +396,106 @@ def run_prefill(args, dev):
     }
 
 
+# --------------------------------------------------------------------------- batched 128k decode
+
+
+BATCH_CFG = dict(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap=128, top_p=64, top_k=4096,
+                 window_size=64, sink_size=4)
+
+
+def run_batched(args, rank, world, dev):
+    """cfg 4: B = 64 sequences, lengths ~ U[65536, 131072] (seeded), Hq 64 / Hkv 8 / Dh 128,
+    bf16, q/k/v ~ N(0, 1), top-64 buckets (4096-token budget), window 64, sinks 4. The
+    sequences are independent: rank r decodes sequences shard_rows(64, world, r) (no
+    collective; total work fixed -> "strong"). A step = one token for every sequence of the
+    rank: one batched-select launch + one read launch, replayed from a CUDA graph. One step
+    reads ~1.1 GB of K/V at N = 1 (> L2): no flush."""
+    import torch
+
+    import lsa_b200 as lsa
+    from lsa_b200 import batched
+    from lsa_b200.index_space import index_keys, index_queries
+
+    B, HQB = 64, 64
+    gen = torch.Generator(device="cpu")
+    gen.manual_seed(SEED + 4)
+    lengths_all = torch.randint(65536, 131073, (B,), generator=gen).tolist()
+    start, end = batched.shard_rows(B, world, rank)
+    lengths = lengths_all[start:end]
+    pcfg = lsa.PortConfig(**BATCH_CFG)
+    Tmax = max(lengths) if lengths else 1
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 4 + rank)
+    nb = len(lengths)
+    q = torch.randn(nb, 1, HQB, DH, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.empty(nb, Tmax, HKV, DH, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(nb, Tmax, HKV, DH, dtype=torch.bfloat16, device=dev)
+    for b in range(nb):  # per sequence, to bound the fp32 temporaries
+        k[b] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
+        v[b] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
+    iq = torch.cat([index_queries(q[b], HKV) for b in range(nb)])
+    bb = batched.concat_buckets([lsa.build_buckets_gpu(index_keys(k[b, :L]), pcfg) for b, L in enumerate(lengths)])
+    pos = torch.tensor([L - 1 for L in lengths], dtype=torch.int32, device=dev)
+    scale = DH ** -0.5
+    stream = torch.cuda.Stream(dev)
+
+    def step():
+        lists, lens = batched.batched_select(iq, pos, bb, pcfg)
+        return lsa.lsa_read(q, k, v, lists[:, None], lens[:, None], scale)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        lists, lens = batched.batched_select(iq, pos, bb, pcfg)
+        stream.synchronize()
+    n_ids = int(lens.long().sum().item())
+    vis = [min((L - 1) // 512 * 8, int(r)) for L, r in zip(lengths, bb.table_rows.tolist())]
+    step_bytes = (sum(vis) * HKV * DH * 2 + nb * pcfg.top_p * pcfg.bucket_cap * 4 + n_ids * HKV * DH * 2 * 2
+                  + nb * (HQB * DH * 2 * 2 + HKV * DH * 4 + lists.shape[1] * 4))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(args.steps):
+            step()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        stream.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+        with ClockSampler(dev.index) as clocks:
+            ev0.record(stream)
+            graph.replay()
+            ev1.record(stream)
+            stream.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    tot = torch.tensor([ms, float(step_bytes), float(nb)], device=dev, dtype=torch.float64)
+    if world > 1:
+        t_max = tot[:1].clone()
+        torch.distributed.all_reduce(t_max, op=torch.distributed.ReduceOp.MAX)
+        sums = tot[1:].clone()
+        torch.distributed.all_reduce(sums)
+        ms, all_bytes, all_seqs = float(t_max.item()), float(sums[0].item()), int(sums[1].item())
+    else:
+        all_bytes, all_seqs = float(step_bytes), nb
+    hbm, tflops, peak_kind = _load_peaks()
+    value = all_bytes / (ms * 1e-3) / 1e9
+    del graph
+    return {
+        "metric": "batched decode select+read GB/s @128k bf16 (64 sequences)", "value": round(value, 2),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v, lengths U[65536, 131072])",
+        "config": {"workload": "batched128k", "batch": B, "sequences_per_rank": nb, "heads_q": HQB,
+                   "heads_kv": HKV, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
+                   "budget_tokens": BATCH_CFG["top_k"], "parallelism": f"sequence-shard{world}",
+                   "l2": "no flush: one step reads > 1 GB of K/V"},
+        "us_per_step": round(ms * 1e3, 2), "sequences": all_seqs, "bytes_per_step": int(all_bytes),
+        "gpu_launches": args.steps * 2, "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
+        "clocks": clocks.summary(),
+    }
+
+
 # --------------------------------------------------------------------------- CPU baseline
 
 
@@ -535,6 +635,8 @@ def main() -> int:
     parser.add_argument("--quick", action="store_true", help="skip e2e, dense and CPU legs (profiling runs)")
     parser.add_argument("--prefill-T", type=int, default=T_CTX, help="prefill leg tokens (0: skip the leg)")
     parser.add_argument("--only-prefill", action="store_true", help="run the prefill leg alone (profiling runs)")
+    parser.add_argument("--workload", default="decode32k", choices=["decode32k", "batched128k"],
+                        help="decode32k (default: + prefill leg) or the 64-sequence 128k batched decode")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     LAYERS = args.layers
@@ -556,6 +658,14 @@ def main() -> int:
         import datetime
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if args.workload == "batched128k":
+        out = run_batched(args, rank, world, dev)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return 0
     if args.only_prefill:
         if rank == 0:
             print(json.dumps(run_prefill(args, dev)), flush=True)

@@ -122,6 +122,21 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
                      int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                      int64_t max_position, cudaStream_t stream);
 
+/* Batched decode (one query row per sequence, sequences of different lengths): the fused
+ * selection of flat_select (pipeline.py:274-316) for every row in one launch, row r reading
+ * its own sequence's buckets = rows [table_off[r], table_off[r] + table_rows[r]) of the
+ * concatenated centroid [sum rows, d] and member [sum rows, cap] tables (member ids are
+ * positions within the row's sequence). max_rows = the largest table_rows[r] (the scratch
+ * key stride). Each row's result equals flat_select on its own sequence's buckets. The
+ * reference has no batched select (its gates build per sequence, gates.py:59). */
+int64_t lsa_select_batched_scratch(int64_t R, int64_t max_rows);
+int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                       int64_t d, const int64_t* table_off, const int32_t* table_rows, int64_t max_rows,
+                       const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members, int64_t cap,
+                       int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists, int32_t* lengths,
+                       void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                       int64_t max_position, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- prefill (tile rows) */
 
 /* Per-64-query-tile selection of the prefill arm. The reference selects per row only

@@ -254,12 +254,21 @@ struct GlobalKeysCg {
 // [r * tile, (r + 1) * tile): the visible count is taken at the tile's first row and the
 // walk runs at the virtual position block_start - 1 with window 0, so a tile's list holds
 // the picked members of closed blocks and the sinks below the tile's open block.
+// Ragged batches (one sequence per row, e.g. batched decode): row r's buckets are rows
+// [table_off[r], table_off[r] + table_rows[r]) of concatenated centroid / member tables;
+// null tables: every row reads the whole table.
 struct RowPos {
     const int32_t* positions;
     int64_t tile, block;
+    const int64_t* table_off;
+    const int32_t* table_rows;
     __device__ __forceinline__ int64_t count_pos(int r) const { return tile ? r * tile : (int64_t)positions[r]; }
     __device__ __forceinline__ int64_t walk_pos(int r) const {
         return tile ? r * tile / block * block - 1 : (int64_t)positions[r];
+    }
+    __device__ __forceinline__ int64_t off(int r) const { return table_off ? table_off[r] : 0; }
+    __device__ __forceinline__ int64_t rows(int r, int64_t N) const {
+        return table_rows ? (int64_t)table_rows[r] : N;
     }
 };
 
@@ -400,10 +409,13 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     pdl_wait();
     pdl_trigger();
     int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t Nr = rp.rows(r, N);  // this row's bucket count (N: the key stride)
+    const TC* cr = c + rp.off(r) * d;
+    const int32_t* mr = members + rp.off(r) * cap;
     // score the grid's columns without waiting for the row's position: the last CTA masks
     // the columns past the row's visible count (the grid covers the widest row)
     int64_t c0 = (int64_t)blockIdx.x * cols_per_cta;
-    int64_t c1 = min(c0 + cols_per_cta, N);
+    int64_t c1 = min(c0 + cols_per_cta, Nr);
     if (c0 < c1) {
         int nchunks = d >> 3;
         float x[CHUNKS][8];
@@ -422,7 +434,7 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
             for (int i = 0; i < 4; ++i) {
                 const int64_t ii = i0 + (int64_t)i * nw;
                 const int64_t n = c0 + (ii + rot < span ? ii + rot : ii + rot - span);
-                part[i] = ii < span ? lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks) : 0.0f;
+                part[i] = ii < span ? lane_partial_regs<TC, CHUNKS>(x, cr + n * d, lane, nchunks) : 0.0f;
             }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -445,9 +457,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     __threadfence();
     int64_t pos = rp.walk_pos(r);
     int64_t vis = rp.count_pos(r) / block * bpb;
-    int count = (int)(vis < N ? vis : N);
+    int count = (int)(vis < Nr ? vis : Nr);
     if (count < 0) count = 0;
-    int k = (int)min((int64_t)top_p, N);
+    int k = (int)min((int64_t)top_p, Nr);
     GlobalKeysCg loader{ws_keys + r * N, count};
     int n2 = next_pow2(max(count, 1));
     int64_t* picks = sbuf;  // sorted keys live at the front of the buffer
@@ -476,11 +488,11 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
         int* mem = reinterpret_cast<int*>(sbuf + k);
-        expand_row_prefetched(picks, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
+        expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
                               lengths + r, scan_smem, mem);
     } else {
         SmemPicks pk{picks};
-        expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+        expand_row(pk, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
                    scan_smem);
     }
 }
@@ -563,6 +575,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int64_t Nr = rp.rows(r, N);  // this row's bucket count
+    const TC* cr = c + rp.off(r) * d;
+    const int32_t* mr = members + rp.off(r) * cap;
     const int cols_per_cta = nw * cpw;
     const int64_t c0 = (int64_t)rank * cols_per_cta;
     // column n's key lands at sbuf[n] of the cluster's rank-0 CTA: every CTA stores its keys
@@ -581,17 +596,17 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
 #pragma unroll
         for (int i = 0; i < kMaxColsPerWarp; ++i) {  // every column's loads in flight together
             int64_t n = c0 + warp + nw * i;
-            bool live = i < cpw && n < N;
-            part[i] = live ? lane_partial_regs<TC, CHUNKS>(x, c + n * d, lane, nchunks) : 0.0f;
+            bool live = i < cpw && n < Nr;
+            part[i] = live ? lane_partial_regs<TC, CHUNKS>(x, cr + n * d, lane, nchunks) : 0.0f;
             // the leader reads the picked buckets' member rows next: pull every scored
             // bucket's row into L2 now
             if (live && lane < lines)
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(members + n * cap + lane * 32));
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(mr + n * cap + lane * 32));
         }
 #pragma unroll
         for (int i = 0; i < kMaxColsPerWarp; ++i) {
             int64_t n = c0 + warp + nw * i;
-            if (i < cpw && n < N) {
+            if (i < cpw && n < Nr) {
                 float p = butterfly_sum(part[i]);
                 if (lane == 0) lead_keys[n] = pack_key(p, (int32_t)n);
             }
@@ -599,10 +614,10 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     }
     cluster.sync();  // every column's key is in the leader's shared memory
     if (rank != 0) return;
-    const int k = (int)min((int64_t)top_p, N);
+    const int k = (int)min((int64_t)top_p, Nr);
     const int64_t pos = rp.walk_pos(r);
     int64_t vis = rp.count_pos(r) / block * bpb;
-    int count = (int)(vis < N ? vis : N);
+    int count = (int)(vis < Nr ? vis : Nr);
     if (count < 0) count = 0;
     const int n2 = next_pow2(max(count, 1));
     for (int t = count + threadIdx.x; t < max(n2, k); t += blockDim.x) sbuf[t] = kEmpty;  // unseen columns
@@ -618,11 +633,11 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
         int* mem = reinterpret_cast<int*>(sbuf + max(k, 32));
-        expand_row_prefetched(picks, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
+        expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
                               lengths + r, scan_smem, mem);
     } else {
         SmemPicks pk{picks};
-        expand_row(pk, k, members, N, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+        expand_row(pk, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
                    scan_smem);
     }
 }
@@ -777,8 +792,8 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     int64_t most = max_position < 0 ? N : (max_position / block * bpb < N ? max_position / block * bpb : N);
     // few rows (decode): one column per warp, the centroid read spread over many SMs;
     // many rows (prefill tiles): one CTA per row scores all its columns (no cross-CTA merge)
-    const bool many_rows = R >= 64;
-    int cols = kFusedThreads / 32;
+    const bool many_rows = R >= 256;
+    int cols = 4 * (kFusedThreads / 32);  // four columns per warp, loads in flight together
     if (many_rows) cols = (int)(((most > 0 ? most : 1) + 15) / 16 * 16);
     int chunks_x = (int)((most + cols - 1) / cols);
     if (chunks_x < 1) chunks_x = 1;
@@ -866,13 +881,28 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
 
 extern "C" {
 
+int64_t lsa_select_batched_scratch(int64_t R, int64_t max_rows) { return lsa_select_fused_scratch(R, max_rows); }
+
+int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
+                       int64_t d, const int64_t* table_off, const int32_t* table_rows, int64_t max_rows,
+                       const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members, int64_t cap,
+                       int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists, int32_t* lengths,
+                       void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                       int64_t max_position, cudaStream_t stream) {
+    if (positions == nullptr || table_off == nullptr || table_rows == nullptr || max_rows < 0) return LSA_ERR_ARG;
+    return select_fused_launch(queries, q_dtype, R, ldq, centroids, c_dtype, max_rows, d,
+                               RowPos{positions, 0, block, table_off, table_rows}, block, bpb, members, cap, top_p,
+                               window, sink, top_k, lists, lengths, scratch, scratch_bytes, counters, n_counters,
+                               max_position, stream);
+}
+
 int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
                      int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
                      int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
                      int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                      int64_t max_position, cudaStream_t stream) {
     if (positions == nullptr) return LSA_ERR_ARG;
-    return select_fused_launch(queries, q_dtype, R, ldq, centroids, c_dtype, N, d, RowPos{positions, 0, block}, block,
+    return select_fused_launch(queries, q_dtype, R, ldq, centroids, c_dtype, N, d, RowPos{positions, 0, block, nullptr, nullptr}, block,
                                bpb, members, cap, top_p, window, sink, top_k, lists, lengths, scratch, scratch_bytes,
                                counters, n_counters, max_position, stream);
 }
@@ -913,7 +943,7 @@ int lsa_tile_select(const void* index_queries, int q_dtype, int64_t T, int64_t l
     int64_t tq_bytes = ((tiles * d * 4 + 255) / 256) * 256;
     int rc = lsa_tile_queries(index_queries, q_dtype, T, ldq, d, tile, tq, stream);
     if (rc) return rc;
-    return select_fused_launch(tq, kF32, tiles, d, centroids, c_dtype, N, d, RowPos{nullptr, tile, block}, block, bpb,
+    return select_fused_launch(tq, kF32, tiles, d, centroids, c_dtype, N, d, RowPos{nullptr, tile, block, nullptr, nullptr}, block, bpb,
                                members, cap, top_p, 0, sink, top_k, lists, lengths, (char*)scratch + tq_bytes,
                                scratch_bytes - tq_bytes, counters, n_counters, (tiles - 1) * tile, stream);
 }

@@ -36,3 +36,13 @@ def regroup_rows(q: torch.Tensor, k: torch.Tensor):
 def make_index_space(q: torch.Tensor, k: torch.Tensor):
     """q [B, T, Hq, D], k [B, T, Hkv, D] -> (index_queries [T, d], index_keys [T, d]) of batch row 0."""
     return regroup_rows(q[0], k[0])
+
+
+def index_keys(k: torch.Tensor) -> torch.Tensor:
+    """k [T, Hkv, D] of one sequence -> unit-row index keys [T, Hkv * D] fp32."""
+    return regroup_rows(k, k)[1]
+
+
+def index_queries(q: torch.Tensor, Hkv: int) -> torch.Tensor:
+    """q [T, Hq, D] -> index queries [T, Hkv * D] fp32 (group means, unnormalised)."""
+    return regroup_rows(q, q[:, :Hkv])[0]
