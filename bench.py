@@ -469,6 +469,24 @@ def run_batched(args, rank, world, dev):
             ev1.record(stream)
             stream.synchronize()
     ms = ev0.elapsed_time(ev1) / args.steps
+    del graph
+
+    def graph_ms(fn):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(args.steps):
+                fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            gr.replay()
+            e0.record(stream)
+            gr.replay()
+            e1.record(stream)
+            stream.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    us_select = graph_ms(lambda: batched.batched_select(iq, pos, bb, pcfg)) * 1e3
+    us_read = graph_ms(lambda: lsa.lsa_read(q, k, v, lists[:, None], lens[:, None], scale)) * 1e3
     tot = torch.tensor([ms, float(step_bytes), float(nb)], device=dev, dtype=torch.float64)
     if world > 1:
         t_max = tot[:1].clone()
@@ -480,7 +498,6 @@ def run_batched(args, rank, world, dev):
         all_bytes, all_seqs = float(step_bytes), nb
     hbm, tflops, peak_kind = _load_peaks()
     value = all_bytes / (ms * 1e-3) / 1e9
-    del graph
     return {
         "metric": "batched decode select+read GB/s @128k bf16 (64 sequences)", "value": round(value, 2),
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
@@ -490,7 +507,8 @@ def run_batched(args, rank, world, dev):
                    "heads_kv": HKV, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
                    "budget_tokens": BATCH_CFG["top_k"], "parallelism": f"sequence-shard{world}",
                    "l2": "no flush: one step reads > 1 GB of K/V"},
-        "us_per_step": round(ms * 1e3, 2), "sequences": all_seqs, "bytes_per_step": int(all_bytes),
+        "us_per_step": round(ms * 1e3, 2), "us_select": round(us_select, 2), "us_read": round(us_read, 2),
+        "sequences": all_seqs, "bytes_per_step": int(all_bytes),
         "gpu_launches": args.steps * 2, "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
         "clocks": clocks.summary(),
     }

@@ -186,6 +186,17 @@ int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positio
                     int64_t size, int64_t nb, int64_t top_level, int64_t beam, int64_t top_p, int32_t* picks,
                     void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream);
 
+/* lsa_tree_select plus the picks' packed keys [R, top_p] (score bits unchanged, bucket column
+ * + col_offset, EMPTY past the picks): a sequence shard's candidates in global bucket ids,
+ * ready for the cross-shard best-first merge (lsa_best_first_keys). No reference counterpart:
+ * the reference decodes one sequence on one device. */
+int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                         int64_t rows, int64_t n_built, const float* const* level_centroids,
+                         const int64_t* const* level_children, const int64_t* level_counts,
+                         const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                         int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
+                         int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- read */
 
 /* Split plan of lsa_sparse_read: splits per (row, KV head), scratch bytes, counters (the
@@ -212,6 +223,23 @@ int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, cons
 int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
                             const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
                             int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream);
+
+/* Sequence-shard partial read (no reference counterpart; the read numerics are
+ * read_kernel_tiled.py:41-89 restricted to this shard's keys): ids are global positions and
+ * k/v hold positions [id_base, id_base + Tk); ids outside are skipped. out32 [B*Tq, Hq, D]
+ * fp32 normalised output over this shard's keys, lse [B*Tq, Hq] their log2-sum-exp of the
+ * scaled scores (-inf when the shard holds none of the row's keys). Scratch / counters as
+ * lsa_sparse_read. */
+int lsa_sparse_read_partial(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
+                            const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
+                            int64_t D, int64_t width, float scale, int64_t id_base, float* out32, float* lse,
+                            void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                            int64_t splits, cudaStream_t stream);
+
+/* The log-sum-exp merge of P shard partials: o [P, n, D] fp32, lse [P, n] -> out [n, D] in
+ * dtype, equal to one read over the union of the shards' (disjoint) key sets. */
+int lsa_merge_partials(const float* o, const float* lse, int64_t P, int64_t n, int64_t D, int dtype, void* out,
+                       cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -129,7 +129,25 @@ struct ReadArgs {
     int64_t Tq, Tk;
     int Hq, Hkv, G, width, splits, span, combine;
     float scale_log2;  // scale * log2(e)
+    // partial mode (sequence shards): ids are global positions, this call's K/V hold
+    // positions [id_base, id_base + Tk); fp32 normalised output and log2-sum-exp per
+    // (row, q head) instead of `out`
+    int id_base;
+    float* out32;
+    float* lse;
 };
+
+// Final write of one output element (and, in partial mode, the row-head's log2-sum-exp).
+template <typename T, int D>
+__device__ __forceinline__ void write_out(const ReadArgs& a, int64_t rq, int e, float O, float M, float L) {
+    const float val = L > 0.0f ? O / L : 0.0f;
+    if (a.out32) {
+        a.out32[rq * D + e] = val;
+        if (e == 0) a.lse[rq] = L > 0.0f ? M + log2f(L) : -INFINITY;
+    } else {
+        reinterpret_cast<T*>(a.out)[rq * D + e] = from_f32<T>(val);
+    }
+}
 
 template <typename T, int D, int GMAX>
 __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
@@ -184,7 +202,7 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     const int my_slot = warp * IDW + (lane % IDW);
     auto load_id = [&](int stage) -> int {  // needs no length: loads overlap the length load
         int at = s0 + stage * STAGE + my_slot;
-        return (issuer && at < s0 + a.span && at < a.width) ? idrow[at] : -1;
+        return (issuer && at < s0 + a.span && at < a.width) ? idrow[at] - a.id_base : -1;
     };
     int id0 = load_id(0), id1 = load_id(1);
     int len = a.lengths[row];
@@ -450,8 +468,7 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
             O += red[(r * GMAX + g) * D + e] * f;
         }
         if (a.combine == kSingle) {
-            float val = L > 0.0f ? O / L : 0.0f;
-            reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
+            write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, M, L);
         } else if (a.combine == kCluster) {
             po[g * D + e] = O;
             if (e == 0) {
@@ -500,8 +517,7 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                     O += peer_o[g * D + e] * f;
                 }
             }
-            float val = L > 0.0f ? O / L : 0.0f;
-            reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
+            write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, M, L);
         }
         cluster.sync();  // keep this CTA's partial alive until every peer has read it
         return;
@@ -518,8 +534,9 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     if (!is_last) return;
     __threadfence();
     // stage the split weights, then every output sums its splits with independent loads
-    float* wts = red;  // [splits][G] weights, then [G] totals
+    float* wts = red;  // [splits][G] weights, then [G] totals and [G] maxima
     float* tot = red + a.splits * G;
+    float* wmax = tot + G;
     for (int i = tid; i < a.splits * G; i += kReadThreads) wts[i] = __ldcg(a.part_ml + ((int64_t)rh * a.splits * G + i) * 2);
     __syncthreads();
     if (tid < G) {
@@ -532,6 +549,7 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
             wts[sp * G + tid] = f;
         }
         tot[tid] = L;
+        wmax[tid] = M;
     }
     __syncthreads();
     for (int o = tid; o < G * D; o += kReadThreads) {
@@ -540,9 +558,7 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
 #pragma unroll 8
         for (int sp = 0; sp < a.splits; ++sp)
             O += wts[sp * G + g] * __ldcg(a.part_o + (((int64_t)rh * a.splits + sp) * G + g) * D + e);
-        float L = tot[g];
-        float val = L > 0.0f ? O / L : 0.0f;
-        reinterpret_cast<T*>(a.out)[((row * a.Hq) + h * G + g) * D + e] = from_f32<T>(val);
+        write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, wmax[g], tot[g]);
     }
 }
 
@@ -691,10 +707,13 @@ static int dispatch_d(const ReadArgs& a, int D, int64_t ctas, cudaStream_t st) {
 int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
                        const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D,
                        int64_t width, float scale, void* out, void* scratch, int64_t scratch_bytes, int32_t* counters,
-                       int64_t n_counters, int64_t splits, cudaStream_t stream) {
+                       int64_t n_counters, int64_t splits, cudaStream_t stream, int64_t id_base = 0,
+                       float* out32 = nullptr, float* lse = nullptr) {
     if (B < 0 || Tq < 0 || Tk < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || width < 0) return LSA_ERR_ARG;
     if (D != 64 && D != 128) return LSA_ERR_ARG;
-    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out | (uintptr_t)scratch) & 15) return LSA_ERR_ARG;
+    if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out | (uintptr_t)scratch | (uintptr_t)out32) & 15)
+        return LSA_ERR_ARG;
+    if ((out32 == nullptr) != (lse == nullptr) || id_base < 0 || id_base > INT32_MAX) return LSA_ERR_ARG;
     int64_t R = B * Tq;
     if (R == 0) return LSA_OK;
     int64_t G = Hq / Hkv;
@@ -712,6 +731,9 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.G = (int)G; a.width = (int)width;
     a.splits = p.splits; a.span = p.span; a.combine = p.combine;
     a.scale_log2 = scale * kLog2e;
+    a.id_base = (int)id_base;
+    a.out32 = out32;
+    a.lse = lse;
     int64_t ctas = R * Hkv * p.splits;
     if (dtype == kBF16) return dispatch_d<__nv_bfloat16>(a, (int)D, ctas, stream);
     if (dtype == kF16) return dispatch_d<__half>(a, (int)D, ctas, stream);
@@ -742,6 +764,72 @@ int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, cons
                     int64_t n_counters, int64_t splits, cudaStream_t stream) {
     return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out, scratch,
                                    scratch_bytes, counters, n_counters, splits, stream);
+}
+
+/* Sequence-shard partial read: lists hold global positions; k/v hold positions
+ * [id_base, id_base + Tk) of every batch row. Writes the fp32 normalised output over this
+ * shard's listed keys and its log2-sum-exp per (row, q head) (-inf: no key here). */
+int lsa_sparse_read_partial(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
+                            const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
+                            int64_t D, int64_t width, float scale, int64_t id_base, float* out32, float* lse,
+                            void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                            int64_t splits, cudaStream_t stream) {
+    if (out32 == nullptr || lse == nullptr) return LSA_ERR_ARG;
+    return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, nullptr,
+                                   scratch, scratch_bytes, counters, n_counters, splits, stream, id_base, out32, lse);
+}
+
+}  // extern "C"
+
+namespace lsa {
+
+// out[i, :] = sum_p o[p, i, :] 2^(lse[p, i] - M) / sum_p 2^(lse[p, i] - M), M = max_p lse[p, i]:
+// the softmax over the union of the parts' disjoint key sets. One warp per row-head.
+template <typename T>
+__global__ void merge_partials_kernel(const float* __restrict__ o, const float* __restrict__ lse, int P, int64_t n,
+                                      int D, T* __restrict__ out) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (i >= n) return;
+    float M = -INFINITY;
+    for (int p = 0; p < P; ++p) M = fmaxf(M, lse[(int64_t)p * n + i]);
+    float W = 0.0f;
+    for (int p = 0; p < P; ++p) {
+        const float x = lse[(int64_t)p * n + i];
+        W += x == -INFINITY ? 0.0f : exp2f(x - M);
+    }
+    for (int e = lane; e < D; e += 32) {
+        float acc = 0.0f;
+        for (int p = 0; p < P; ++p) {
+            const float x = lse[(int64_t)p * n + i];
+            if (x != -INFINITY) acc += o[((int64_t)p * n + i) * D + e] * exp2f(x - M);
+        }
+        out[i * D + e] = from_f32<T>(W > 0.0f ? acc / W : 0.0f);
+    }
+}
+
+}  // namespace lsa
+
+extern "C" {
+
+/* Merge P shard partials (o [P, n, D] fp32 normalised, lse [P, n] log2-sum-exp) into
+ * out [n, D] of dtype (the result of one read over the union of the shards' keys). */
+int lsa_merge_partials(const float* o, const float* lse, int64_t P, int64_t n, int64_t D, int dtype, void* out,
+                       cudaStream_t stream) {
+    if (P <= 0 || n < 0 || D <= 0) return LSA_ERR_ARG;
+    if (n == 0) return LSA_OK;
+    const unsigned grid = (unsigned)((n * 32 + 255) / 256);
+    if (dtype == lsa::kBF16)
+        lsa::merge_partials_kernel<__nv_bfloat16>
+            <<<grid, 256, 0, stream>>>(o, lse, (int)P, n, (int)D, (__nv_bfloat16*)out);
+    else if (dtype == lsa::kF16)
+        lsa::merge_partials_kernel<__half><<<grid, 256, 0, stream>>>(o, lse, (int)P, n, (int)D, (__half*)out);
+    else if (dtype == lsa::kF32)
+        lsa::merge_partials_kernel<float><<<grid, 256, 0, stream>>>(o, lse, (int)P, n, (int)D, (float*)out);
+    else
+        return LSA_ERR_ARG;
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
 }
 
 }  // extern "C"

@@ -65,6 +65,8 @@ struct TreeLevelArgs {
     int32_t* carried_n_out;      // [R]
     int carry_cap;
     int32_t* picks;              // [R, top_p] (L == 0)
+    int64_t* pick_keys;          // [R, top_p] packed keys of the picks, column + col_offset (may be null)
+    int64_t col_offset;
     int64_t* ws_keys;            // [R, cand_cap]
     int cand_cap;
     int32_t* tickets;            // [R]
@@ -137,8 +139,17 @@ __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
         kept = n_cand < a.keep ? n_cand : a.keep;
     }
     if (a.L == 0) {
-        for (int i = threadIdx.x; i < a.keep; i += blockDim.x)
+        for (int i = threadIdx.x; i < a.keep; i += blockDim.x) {
             a.picks[(int64_t)r * a.keep + i] = i < kept ? key_bucket(tsm[i]) : -1;
+            if (a.pick_keys) {  // same score bits, column rebased (e.g. to a global bucket id)
+                int64_t key = kEmpty;
+                if (i < kept) {
+                    const uint64_t hi = (uint64_t)tsm[i] & 0xFFFFFFFF00000000ull;
+                    key = (int64_t)(hi | (uint32_t)(0x7FFFFFFF - (key_bucket(tsm[i]) + (int32_t)a.col_offset)));
+                }
+                a.pick_keys[(int64_t)r * a.keep + i] = key;
+            }
+        }
     } else {
         int S = (int)a.size;
         for (int i = threadIdx.x; i < kept * S; i += blockDim.x) {
@@ -194,11 +205,30 @@ int lsa_tree_plan(int64_t R, int64_t n_built, const int64_t* level_counts, int64
 
 // Tree beam picks [R, top_p] int32 (-1 padded). level_centroids / level_children /
 // level_counts are HOST arrays of n_built entries (device pointers / node counts).
+int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                         int64_t rows, int64_t n_built, const float* const* level_centroids,
+                         const int64_t* const* level_children, const int64_t* level_counts,
+                         const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                         int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
+                         int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream);
+
 int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
                     int64_t rows, int64_t n_built, const float* const* level_centroids,
                     const int64_t* const* level_children, const int64_t* level_counts, const float* bucket_centroids,
                     int64_t size, int64_t nb, int64_t top_level, int64_t beam, int64_t top_p, int32_t* picks,
                     void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream) {
+    return lsa_tree_select_keys(q, R, d, positions, block, bpb, rows, n_built, level_centroids, level_children,
+                                level_counts, bucket_centroids, size, nb, top_level, beam, top_p, picks, nullptr, 0,
+                                scratch, scratch_bytes, counters, n_counters, stream);
+}
+
+int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                         int64_t rows, int64_t n_built, const float* const* level_centroids,
+                         const int64_t* const* level_children, const int64_t* level_counts,
+                         const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                         int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
+                         int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream) {
+    if (col_offset < 0 || col_offset + rows > INT32_MAX) return LSA_ERR_ARG;
     if (d <= 0 || d % 8 || d > 2048 || ((uintptr_t)q & 15) || top_level > kTreeMaxLevels || n_built > top_level)
         return LSA_ERR_ARG;
     if (top_p <= 0 || top_p > kTreeSortCap || block <= 0) return LSA_ERR_ARG;
@@ -218,6 +248,8 @@ int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positio
     a.tickets = counters;
     a.status = counters + R;
     a.picks = picks;
+    a.pick_keys = pick_keys;
+    a.col_offset = col_offset;
     int chunks = (int)((d / 8 + 31) / 32);
     int smem = next_pow2(p.cand_cap) * 8;
     if (smem < 1024) smem = 1024;

@@ -61,6 +61,11 @@ SIGNATURES = {
     "lsa_tile_select": (_INT, [_P, _INT, _I, _I, _I, _P, _INT, _I, _I, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _I,
                                _P, _I, _P]),
     "lsa_sparse_prefill": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P]),
+    "lsa_tree_select_keys": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I,
+                                    _P, _I, _P, _I, _P]),
+    "lsa_sparse_read_partial": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _I, _P, _P, _P, _I,
+                                       _P, _I, _I, _P]),
+    "lsa_merge_partials": (_INT, [_P, _P, _I, _I, _I, _INT, _P, _P]),
     "lsa_tree_plan": (_INT, [_I, _I, _P, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_tree_select": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P,
                                _I, _P]),
