@@ -514,6 +514,102 @@ def run_batched(args, rank, world, dev):
     }
 
 
+# --------------------------------------------------------------------------- tree 1M decode
+
+
+TREE_CFG = dict(cluster_block_size=1024, pool_size=8, bucket_size=128, bucket_cap=256, top_p=64, top_k=8192,
+                window_size=128, sink_size=4, node_bucket_size=16, top_level=2, node_cluster_block_size=64,
+                beam_width=64)
+
+
+def run_tree1m(args, rank, world, dev):
+    """cfg 5: B = 4 sequences of 1,048,576 tokens, Hq 32 / Hkv 8 / Dh 128, bf16, drift keys,
+    128-token buckets (8 per 1024-token block), nodes of 16 buckets, two levels, beam 64,
+    top-64 buckets (8192-token budget), window 128, sinks 4; pools of 8 (a 1024-token block
+    of pools of 4 would exceed the Ward merge's 128 pools). Each rank holds a contiguous,
+    block-aligned 1/N of every sequence and its shard index; a step decodes one token per
+    sequence through lsa_b200.seqshard (candidate all-gather, best-first merge, partial
+    reads, log-sum-exp merge over NCCL). Total work fixed -> "strong". Eager launches and
+    collectives, timed with CUDA events, max over ranks."""
+    import torch
+
+    import lsa_b200 as lsa
+    from lsa_b200 import seqshard, synthetic
+    from lsa_b200.index_space import index_keys, index_queries
+
+    B, C = 4, args.tree_ctx
+    pcfg = lsa.PortConfig(**TREE_CFG)
+    s0, s1 = seqshard.shard_bounds(C, world, rank, TREE_CFG["cluster_block_size"])
+    n = s1 - s0
+    g = torch.Generator(device=dev)
+    g.manual_seed(SEED + 5 + rank)
+    q = torch.randn(B, 1, HQ, DH, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
+    gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
+    shards = []
+    for b in range(B):
+        k[b] = synthetic.drift_keys(n, HKV, DH, g, dev)[0].to(torch.bfloat16)
+        v[b] = torch.randn(n, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
+        si = seqshard.build_shard_index(index_keys(k[b]), s0, pcfg)
+        rows = gather(torch.tensor([si.buckets.rows], dtype=torch.int64, device=dev))[:, 0].tolist()
+        mine = seqshard.local_global_members(si)
+        padded = torch.full((max(rows), mine.shape[1]), -1, dtype=torch.int32, device=dev)
+        padded[: mine.shape[0]] = mine
+        tables = gather(padded)
+        si.bucket_offset = sum(rows[:rank])
+        si.members_global = torch.cat([tables[r][: rows[r]] for r in range(len(rows))]).contiguous()
+        shards.append(si)
+    # a 1-GPU run holds the whole sequence: its queries decode the last position
+    iq = [index_queries(q[b], HKV) for b in range(B)]
+    pos = torch.full((1,), C - 1, dtype=torch.int32, device=dev)
+    scale = DH ** -0.5
+
+    def step():
+        return [seqshard.seqshard_decode(q[b:b + 1], k[b:b + 1], v[b:b + 1], iq[b], pos, shards[b], pcfg, gather,
+                                         scale) for b in range(B)]
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clocks:
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    # algorithmic bytes of a step over all ranks: listed K/V rows + scored centroids (beam)
+    width_ids = TREE_CFG["top_k"] + TREE_CFG["window_size"] + TREE_CFG["sink_size"]
+    kv_bytes = B * width_ids * HKV * DH * 2 * 2
+    levels_rows = sum(lv.centroids.shape[0] for si in shards for lv in si.hierarchy.levels)
+    cand_bytes = B * (TREE_CFG["beam_width"] * TREE_CFG["node_bucket_size"] * 2 + TREE_CFG["node_cluster_block_size"])
+    cand_bytes *= HKV * DH * 4 * world
+    step_bytes = kv_bytes + cand_bytes
+    hbm, tflops, peak_kind = _load_peaks()
+    value = step_bytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": "tree decode select+read µs/step @1M bf16 (4 sequences)", "value": round(ms * 1e3, 2),
+        "unit": "us/step", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded drift keys, N(0,1) q/v)",
+        "config": {"workload": "tree1m", "batch": B, "context": C, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
+                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": "NCCL all-gather x3/seq",
+                   **{k2: TREE_CFG[k2] for k2 in ("bucket_size", "top_p", "top_k", "beam_width")},
+                   "l2": "no flush: 4 x 1M-token caches (16 GiB) >> L2"},
+        "effective_gbs": round(value, 2), "step_roofline_frac": round(value / world / hbm, 4),
+        "bytes_per_step": step_bytes, "hierarchy_nodes": levels_rows, "peak_kind": peak_kind,
+        "clocks": clocks.summary(),
+    }
+
+
 # --------------------------------------------------------------------------- CPU baseline
 
 
@@ -653,8 +749,10 @@ def main() -> int:
     parser.add_argument("--quick", action="store_true", help="skip e2e, dense and CPU legs (profiling runs)")
     parser.add_argument("--prefill-T", type=int, default=T_CTX, help="prefill leg tokens (0: skip the leg)")
     parser.add_argument("--only-prefill", action="store_true", help="run the prefill leg alone (profiling runs)")
-    parser.add_argument("--workload", default="decode32k", choices=["decode32k", "batched128k"],
-                        help="decode32k (default: + prefill leg) or the 64-sequence 128k batched decode")
+    parser.add_argument("--workload", default="decode32k", choices=["decode32k", "batched128k", "tree1m"],
+                        help="decode32k (default: + prefill leg), the 64-sequence 128k batched decode, or the "
+                             "sequence-sharded 1M tree decode")
+    parser.add_argument("--tree-ctx", type=int, default=1 << 20, help="tree1m context length")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     LAYERS = args.layers
@@ -676,8 +774,8 @@ def main() -> int:
         import datetime
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if args.workload == "batched128k":
-        out = run_batched(args, rank, world, dev)
+    if args.workload in ("batched128k", "tree1m"):
+        out = (run_batched if args.workload == "batched128k" else run_tree1m)(args, rank, world, dev)
         if rank == 0:
             print(json.dumps(out), flush=True)
         if world > 1:
