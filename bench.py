@@ -405,11 +405,14 @@ BATCH_CFG = dict(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap
 
 def run_batched(args, rank, world, dev):
     """cfg 4: B = 64 sequences, lengths ~ U[65536, 131072] (seeded), Hq 64 / Hkv 8 / Dh 128,
-    bf16, q/k/v ~ N(0, 1), top-64 buckets (4096-token budget), window 64, sinks 4. The
-    sequences are independent: rank r decodes sequences shard_rows(64, world, r) (no
-    collective; total work fixed -> "strong"). A step = one token for every sequence of the
-    rank: one batched-select launch + one read launch, replayed from a CUDA graph. One step
-    reads ~1.1 GB of K/V at N = 1 (> L2): no flush."""
+    bf16, q/k/v ~ N(0, 1), top-64 buckets (4096-token budget), window 64, sinks 4.
+    Sharding (no collective either way; total work fixed -> "strong"):
+      heads (default, the configuration's own): every rank holds all 64 sequences' index
+        (centroids and members, replicated) and selects for all of them - the selection is
+        shared by the heads - then reads only its Hkv / N KV heads (and their q heads);
+      sequences: rank r owns sequences shard_rows(64, world, r) with all their heads.
+    A step = one token for every sequence: one batched-select launch + one read launch,
+    replayed from a CUDA graph. One step reads ~1.1 GB of K/V at N = 1 (> L2): no flush."""
     import torch
 
     import lsa_b200 as lsa
@@ -417,27 +420,41 @@ def run_batched(args, rank, world, dev):
     from lsa_b200.index_space import index_keys, index_queries
 
     B, HQB = 64, 64
+    by_heads = args.batched_shard == "heads"
+    if by_heads and HKV % world:
+        raise ValueError(f"head sharding needs {HKV} KV heads to divide over {world} ranks")
     gen = torch.Generator(device="cpu")
     gen.manual_seed(SEED + 4)
     lengths_all = torch.randint(65536, 131073, (B,), generator=gen).tolist()
-    start, end = batched.shard_rows(B, world, rank)
+    start, end = (0, B) if by_heads else batched.shard_rows(B, world, rank)
     lengths = lengths_all[start:end]
+    h0, h1 = (rank * HKV // world, (rank + 1) * HKV // world) if by_heads else (0, HKV)
+    G = HQB // HKV
     pcfg = lsa.PortConfig(**BATCH_CFG)
     Tmax = max(lengths) if lengths else 1
-    g = torch.Generator(device=dev)
-    g.manual_seed(SEED + 4 + rank)
     nb = len(lengths)
-    q = torch.randn(nb, 1, HQB, DH, generator=g, device=dev).to(torch.bfloat16)
-    k = torch.empty(nb, Tmax, HKV, DH, dtype=torch.bfloat16, device=dev)
-    v = torch.empty(nb, Tmax, HKV, DH, dtype=torch.bfloat16, device=dev)
-    for b in range(nb):  # per sequence, to bound the fp32 temporaries
-        k[b] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
-        v[b] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
-    iq = torch.cat([index_queries(q[b], HKV) for b in range(nb)])
-    bb = batched.concat_buckets([lsa.build_buckets_gpu(index_keys(k[b, :L]), pcfg) for b, L in enumerate(lengths)])
+    q = torch.empty(nb, 1, (h1 - h0) * G, DH, dtype=torch.bfloat16, device=dev)
+    k = torch.empty(nb, Tmax, h1 - h0, DH, dtype=torch.bfloat16, device=dev)
+    v = torch.empty(nb, Tmax, h1 - h0, DH, dtype=torch.bfloat16, device=dev)
+    iqs, per_seq = [], []
+    for i, L in enumerate(lengths):  # per sequence (seeded by the sequence, not the rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED + 4 + 1000 * (start + i))
+        qf = torch.randn(1, HQB, DH, generator=g, device=dev).to(torch.bfloat16)
+        kf = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
+        q[i] = qf[:, h0 * G:h1 * G]
+        k[i] = kf[:, h0:h1]
+        v[i] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)[:, h0:h1]
+        iqs.append(index_queries(qf, HKV))
+        per_seq.append(lsa.build_buckets_gpu(index_keys(kf[:L]), pcfg))
+        del kf
+    iq = torch.cat(iqs)
+    bb = batched.concat_buckets(per_seq)
+    del per_seq
     pos = torch.tensor([L - 1 for L in lengths], dtype=torch.int32, device=dev)
     scale = DH ** -0.5
     stream = torch.cuda.Stream(dev)
+    hkv_r = h1 - h0
 
     def step():
         lists, lens = batched.batched_select(iq, pos, bb, pcfg)
@@ -450,8 +467,11 @@ def run_batched(args, rank, world, dev):
         stream.synchronize()
     n_ids = int(lens.long().sum().item())
     vis = [min((L - 1) // 512 * 8, int(r)) for L, r in zip(lengths, bb.table_rows.tolist())]
-    step_bytes = (sum(vis) * HKV * DH * 2 + nb * pcfg.top_p * pcfg.bucket_cap * 4 + n_ids * HKV * DH * 2 * 2
-                  + nb * (HQB * DH * 2 * 2 + HKV * DH * 4 + lists.shape[1] * 4))
+    # the selection's bytes count once per step (replicated selections are not extra work)
+    sel_bytes = sum(vis) * HKV * DH * 2 + nb * pcfg.top_p * pcfg.bucket_cap * 4 + nb * lists.shape[1] * 4
+    if by_heads and rank != 0:
+        sel_bytes = 0
+    step_bytes = sel_bytes + n_ids * hkv_r * DH * 2 * 2 + nb * (hkv_r * G * DH * 2 * 2 + HKV * DH * 4)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(args.steps):
@@ -504,8 +524,9 @@ def run_batched(args, rank, world, dev):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v, lengths U[65536, 131072])",
         "config": {"workload": "batched128k", "batch": B, "sequences_per_rank": nb, "heads_q": HQB,
-                   "heads_kv": HKV, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
-                   "budget_tokens": BATCH_CFG["top_k"], "parallelism": f"sequence-shard{world}",
+                   "heads_kv": HKV, "heads_kv_per_rank": hkv_r, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
+                   "budget_tokens": BATCH_CFG["top_k"],
+                   "parallelism": f"{'kv-head' if by_heads else 'sequence'}-shard{world}",
                    "l2": "no flush: one step reads > 1 GB of K/V"},
         "us_per_step": round(ms * 1e3, 2), "us_select": round(us_select, 2), "us_read": round(us_read, 2),
         "sequences": all_seqs, "bytes_per_step": int(all_bytes),
@@ -753,6 +774,8 @@ def main() -> int:
                         help="decode32k (default: + prefill leg), the 64-sequence 128k batched decode, or the "
                              "sequence-sharded 1M tree decode")
     parser.add_argument("--tree-ctx", type=int, default=1 << 20, help="tree1m context length")
+    parser.add_argument("--batched-shard", default="heads", choices=["heads", "sequences"],
+                        help="batched128k over ranks: by KV head (selection replicated) or by sequence")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     LAYERS = args.layers
@@ -772,6 +795,9 @@ def main() -> int:
     torch.cuda.set_device(dev)
     if world > 1:
         import datetime
+
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     if args.workload in ("batched128k", "tree1m"):
