@@ -137,6 +137,26 @@ int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq,
                        void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                        int64_t max_position, cudaStream_t stream);
 
+/* ---------------------------------------------------------------- fused decode */
+
+/* flat_select (LSA_SELECT_IMPL=fused scoring with bf16 queries and centroids,
+ * pipeline.py:274-316) followed by lsa_read (read_kernel_tiled.py:41-89) for R <= 4 query
+ * rows of ONE sequence, in one cooperative launch (one CTA per SM): grid-wide scoring, one
+ * bounded grid barrier, per-CTA top-32 and expansion into shared memory, split reads with a
+ * ticket merge. top_p <= 32, D = 128, Hq / Hkv in {4, 8}, dtype bf16 or fp16; q [R, Hq, D],
+ * k/v [Tk, Hkv, D]. lists [R, top_k + window + sink] / lengths [R] receive the read lists
+ * when non-null (bit-equal to flat_select). Scratch and counters (zero at rest; the kernel
+ * leaves them zero) from lsa_decode_fused_plan. No reference counterpart: the reference runs
+ * select and read as separate launches (its ROADMAP item 3 names this fusion). */
+int lsa_decode_fused_plan(int64_t R, int64_t Hq, int64_t Hkv, int64_t N, int64_t cap, int64_t width,
+                          int64_t* scratch_bytes, int64_t* n_counters);
+int lsa_decode_fused(const void* index_queries, int64_t R, int64_t ldq, const void* centroids, int64_t N, int64_t d,
+                     const int32_t* members, int64_t cap, const int32_t* positions, int64_t block, int64_t bpb,
+                     int64_t top_p, int64_t window, int64_t sink, int64_t top_k, const void* q, const void* k,
+                     const void* v, int dtype, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D, float scale, void* out,
+                     int32_t* lists, int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters,
+                     int64_t n_counters, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- prefill (tile rows) */
 
 /* Per-64-query-tile selection of the prefill arm. The reference selects per row only

@@ -25,6 +25,7 @@ device status word to raise on an infeasible Ward merge.
 
 from __future__ import annotations
 
+import ctypes
 import os
 from dataclasses import dataclass, field
 
@@ -393,6 +394,44 @@ def tree_select(index_queries, positions, buckets, hierarchy, config, top_k=None
     from ._tree import tree_select_batched
 
     return tree_select_batched(index_queries, positions, buckets, hierarchy, config, top_k)
+
+
+def decode_fused(q, k, v, index_queries, positions, buckets, config, scale=None, return_lists=False):
+    """flat_select + lsa_read for the decode rows of one sequence in ONE launch.
+
+    q [1, R, Hq, 128] (R <= 4 rows at ``positions``), k/v [1, Tk, Hkv, 128] bf16/fp16,
+    index_queries [R, d]. Same lists as ``flat_select`` (bf16 scoring), same read as
+    ``lsa_read``; ``return_lists`` also returns (lists, lengths)."""
+    require_cuda(q, k, v, index_queries, positions, what="decode_fused")
+    if q.dtype not in (torch.bfloat16, torch.float16) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("decode_fused reads bf16 or fp16 q/k/v")
+    B, R, Hq, D = q.shape
+    if B != 1 or k.shape[0] != 1:
+        raise ValueError("decode_fused decodes rows of one sequence (batch 1)")
+    Tk, Hkv = k.shape[1], k.shape[2]
+    iq = index_queries.to(torch.bfloat16).contiguous()
+    c = buckets.centroids.contiguous()
+    N, d = c.shape
+    width = config.top_k + config.window_size + config.sink_size
+    dev = q.device
+    out = torch.empty_like(q)
+    lists = torch.empty(R, width, dtype=torch.int32, device=dev) if return_lists else None
+    lengths = torch.empty(R, dtype=torch.int32, device=dev) if return_lists else None
+    L = lib()
+    sb, nc = ctypes.c_int64(), ctypes.c_int64()
+    check(L.lsa_decode_fused_plan(R, Hq, Hkv, N, buckets.members.shape[1], width, ctypes.byref(sb),
+                                  ctypes.byref(nc)), "decode_fused")
+    sc = _lib.scratch(sb.value, dev)
+    ct = _lib.counters(nc.value, dev)
+    pos = positions.to(torch.int32).contiguous()
+    scale = D ** -0.5 if scale is None else float(scale)
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    check(L.lsa_decode_fused(ptr(iq), R, d, ptr(c), N, d, ptr(buckets.members), buckets.members.shape[1], ptr(pos),
+                             config.cluster_block_size, config.block_bucket_count, config.top_p, config.window_size,
+                             config.sink_size, config.top_k, ptr(qc), ptr(kc), ptr(vc), _lib.DTYPE_CODE[q.dtype], Tk,
+                             Hq, Hkv, D, scale, ptr(out), ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct),
+                             ct.numel(), stream_of(q)), "decode_fused")
+    return (out, lists, lengths) if return_lists else out
 
 
 # ------------------------------------------------------------------ read
