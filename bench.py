@@ -169,12 +169,20 @@ def run_b200(args, rank, world, dev):
     def read(L, lists, lengths):
         return lsa.lsa_read(L["q"], L["k"], L["v"], lists[None], lengths[None], scale)
 
-    def step():
+    def fused(L):
+        return pipeline.decode_fused(L["q"], L["k"], L["v"], L["iq"], L["pos"], L["buckets"], pcfg, scale)
+
+    def split_step():
         outs = []
         for L in layers:
             lists, lengths = select(L)
             outs.append(read(L, lists, lengths))
         return outs
+
+    def step():
+        if args.decode_impl == "split":
+            return split_step()
+        return [fused(L) for L in layers]
 
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
@@ -197,6 +205,19 @@ def run_b200(args, rank, world, dev):
     with torch.cuda.graph(graph, stream=stream):
         for _ in range(args.steps):
             step()
+    split_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(split_graph, stream=stream):
+        for _ in range(args.steps):
+            split_step()
+    fused_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for L in layers:
+            fused(L)
+        stream.synchronize()
+    with torch.cuda.graph(fused_graph, stream=stream):
+        for _ in range(args.steps):
+            for L in layers:
+                fused(L)
     read_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(read_graph, stream=stream):
         for _ in range(args.steps):
@@ -231,6 +252,8 @@ def run_b200(args, rank, world, dev):
         ms_total = timed(graph)
     ms_read = timed(read_graph)
     ms_select = timed(select_graph)
+    ms_split = timed(split_graph)
+    ms_fused = timed(fused_graph)
     if world > 1:
         t = torch.tensor([ms_total], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -251,8 +274,11 @@ def run_b200(args, rank, world, dev):
         outs = []
         for i, L in enumerate(layers):
             iq, _ = regroup_rows(qd[i, 0], k_last[i])
-            lists, lengths = lsa.flat_select(iq, L["pos"], L["buckets"], pcfg)
-            outs.append(lsa.lsa_read(qd[i], L["k"], L["v"], lists[None], lengths[None], scale))
+            if args.decode_impl == "split":
+                lists, lengths = lsa.flat_select(iq, L["pos"], L["buckets"], pcfg)
+                outs.append(lsa.lsa_read(qd[i], L["k"], L["v"], lists[None], lengths[None], scale))
+            else:
+                outs.append(pipeline.decode_fused(qd[i], L["k"], L["v"], iq, L["pos"], L["buckets"], pcfg, scale))
         out_host.copy_(torch.stack(outs), non_blocking=True)
 
     e2e_ms, us_dense = float("nan"), float("nan")
@@ -286,6 +312,17 @@ def run_b200(args, rank, world, dev):
 
     hbm, tflops, peak_kind = _load_peaks()
     read_gbs = read_bytes_per_launch / (us_read * 1e-6) / 1e9
+    fused_impl = args.decode_impl != "split"
+    if fused_impl:  # the step is one fused kernel per layer: its bytes over its time
+        roof = {"bound": "hbm", "kernel": "lsa::fused_decode_kernel", "achieved": round(value / world, 1),
+                "peak": hbm, "unit": "GB/s", "frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
+                "traffic": _traffic_from_profile("fused_decode_32k.md"),
+                "bytes_per_launch": round(step_bytes / LAYERS)}
+    else:
+        roof = {"bound": "hbm", "kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1),
+                "peak": hbm, "unit": "GB/s", "frac": round(read_gbs / hbm, 4), "peak_kind": peak_kind,
+                "traffic": _traffic_from_profile("sparse_read_decode32k.md"),
+                "bytes_per_launch": round(read_bytes_per_launch)}
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
@@ -293,19 +330,20 @@ def run_b200(args, rank, world, dev):
         "config": {"workload": "decode32k", "layers_per_step": LAYERS, "context": T_CTX, "batch": 1,
                    "heads_q": HQ, "heads_kv": HKV, "head_dim": DH, "bucket_size": CFG["bucket_size"],
                    "top_p_buckets": CFG["top_p"], "budget_tokens": CFG["top_k"], "window": CFG["window_size"],
-                   "sink": CFG["sink_size"], "select_impl": "fused", "parallelism": f"replicas{world}",
+                   "sink": CFG["sink_size"], "decode_impl": args.decode_impl, "parallelism": f"replicas{world}",
                    "l2": "no flush: 32 independent 32k caches, each step touches 32 x ~9.7 MB > 2x L2"},
         "us_per_select_read": round(ms_per_step / LAYERS * 1e3, 3),
+        "us_per_select_read_split": round(ms_split / args.steps / LAYERS * 1e3, 3),
+        "us_per_select_read_fused": round(ms_fused / args.steps / LAYERS * 1e3, 3),
         "us_per_select": round(us_select, 3), "us_per_read": round(us_read, 3),
+        "read_roofline": {"kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
+                          "frac": round(read_gbs / hbm, 4)},
         "dense_us_per_decode": round(us_dense, 3),
         "speedup_vs_dense_decode": (round(us_dense / (ms_per_step / LAYERS * 1e3), 3)
                                     if us_dense == us_dense else None),
         "bytes_per_step": step_bytes, "keys_read_per_step": n_ids,
-        "gpu_launches": args.steps * LAYERS * 2,
-        "roofline": {"bound": "hbm", "kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1),
-                     "peak": hbm, "unit": "GB/s", "frac": round(read_gbs / hbm, 4), "peak_kind": peak_kind,
-                     "traffic": _traffic_from_profile("sparse_read_decode32k.md"),
-                     "bytes_per_launch": round(read_bytes_per_launch)},
+        "gpu_launches": args.steps * LAYERS * (1 if fused_impl else 2),
+        "roofline": roof,
         "step_roofline_frac": round(value / world / hbm, 4),
         "e2e": None if e2e_ms != e2e_ms else {"value": round(world * step_bytes / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(q_host.numel() * 2),
@@ -774,6 +812,8 @@ def main() -> int:
                         help="decode32k (default: + prefill leg), the 64-sequence 128k batched decode, or the "
                              "sequence-sharded 1M tree decode")
     parser.add_argument("--tree-ctx", type=int, default=1 << 20, help="tree1m context length")
+    parser.add_argument("--decode-impl", default="split", choices=["split", "fused"],
+                        help="decode32k step: the select and read launches (default), or one fused launch")
     parser.add_argument("--batched-shard", default="heads", choices=["heads", "sequences"],
                         help="batched128k over ranks: by KV head (selection replicated) or by sequence")
     args = parser.parse_args()

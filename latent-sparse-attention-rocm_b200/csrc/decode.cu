@@ -11,15 +11,17 @@
 //      tree), stages the picked buckets' members and builds the row's read list in shared
 //      memory (the expansion walk: members with sink <= id < window_start in pick order,
 //      first top_k, then the window, then the sinks) - redundantly, so no second barrier;
-//   D  the CTA reads its split of the list for one KV head (16-byte vector loads of the K
-//      and V rows, 16 lanes per row, online softmax for the G query heads), merges its
-//      warps, and the last CTA of the (row, KV head) merges the splits (atomic ticket).
+//   D  the CTA reads its split of the list for one KV head: the K and V rows go to shared
+//      memory by 16-byte cp.async, two 64-key stages in flight, then 16 lanes per row
+//      with an online softmax for the G query heads; the CTA merges its warps, and the
+//      last CTA of the (row, KV head) merges the splits (atomic ticket).
 // Results equal flat_select + lsa_read: the list is the same walk (bit-exact, written out
 // when asked), the read the same math in another summation order.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "topk.cuh"
+#include "umma.cuh"
 
 namespace lsa {
 namespace {
@@ -27,6 +29,7 @@ namespace {
 constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecMaxRows = 4;
+constexpr int kDecChunk = 64;  // K/V rows per shared-memory stage
 constexpr uint64_t kDecWaitNs = 1000000000ull;
 
 struct FusedDecodeArgs {
@@ -128,47 +131,60 @@ __global__ void __launch_bounds__(kDecThreads) fused_decode_kernel(const FusedDe
     const int64_t pos = a.positions[r];
 
     // ------------------------------------------------------------------ C: top-32 + list
-    int64_t* skeys = reinterpret_cast<int64_t*>(dsm);                                  // [N]
-    int32_t* mem = reinterpret_cast<int32_t*>(dsm + ((a.N * 8 + 15) / 16) * 16);       // [32, cap]
-    int32_t* list = mem + 32 * a.cap;                                                  // [width]
+    // shared memory: [keys N x 8 | members 32 x cap x 4 | list width x 4 | K/V 2 stages];
+    // the CTA merge reuses it from the start once the read is done
+    int64_t* skeys = reinterpret_cast<int64_t*>(dsm);
+    int32_t* mem = reinterpret_cast<int32_t*>(dsm + ((a.N * 8 + 15) / 16) * 16);
+    int32_t* list = mem + 32 * a.cap;
+    T* kvs = reinterpret_cast<T*>(dsm + (((a.N * 8 + 15) / 16) * 16 + (int64_t)(32 * a.cap + a.width) * 4 + 15) / 16 *
+                                            16);  // [2][kDecChunk][2][128]
     {
         const int64_t vis = pos / a.block * a.bpb;
         const int count = (int)(vis < a.N ? (vis < 0 ? 0 : vis) : a.N);
         for (int i = threadIdx.x; i < count; i += kDecThreads) skeys[i] = __ldcg(a.keys + (int64_t)r * a.N + i);
         __syncthreads();
         block_top32_desc(skeys, count, tl, picks);
-        const int kp = (int)min((int64_t)a.top_p, a.N);  // picks walked (<= 32)
-        // stage the picked buckets' member rows (prefetched into L2 during scoring)
-        for (int i = threadIdx.x; i < 32 * a.cap; i += kDecThreads) {
-            const int p = i / a.cap, slot = i % a.cap;
-            const int32_t b = p < kp ? key_bucket(picks[p]) : -1;
-            mem[i] = b >= 0 ? __ldg(a.members + (int64_t)b * a.cap + slot) : -1;
+        const int kp = (int)min((int64_t)a.top_p, a.N);
+        // picks past the live keys are EMPTY and sort last: the valid picks are a prefix
+        int kv = 0;
+        for (int p = 0; p < kp; ++p) kv += key_bucket(picks[p]) >= 0;
+        // stage the picked buckets' member rows with 16-byte copies, all in flight at once
+        const int q4 = a.cap / 4;
+        for (int i = threadIdx.x; i < kv * q4; i += kDecThreads) {
+            const int p = i / q4, c4 = i % q4;
+            cp_async16(smem_u32(mem + p * a.cap + c4 * 4), a.members + (int64_t)key_bucket(picks[p]) * a.cap + c4 * 4,
+                       16u);
         }
+        cp_async_wait_all();
         __syncthreads();
         int64_t ws = pos + 1 - a.window;
         if (ws < 0) ws = 0;
-        // kept members per pick (sink <= id < ws), in slot order
+        // kept members per pick (sink <= id < ws), then their offsets by a warp scan
         for (int p = warp; p < 32; p += kDecWarps) {
             int c = 0;
-            for (int s0 = 0; s0 < a.cap; s0 += 32) {
-                const int slot = s0 + lane;
-                const int id = slot < a.cap ? mem[p * a.cap + slot] : -1;
-                c += __popc(__ballot_sync(0xFFFFFFFFu, id >= a.sink && (int64_t)id < ws));
+            if (p < kv) {
+                for (int s0 = 0; s0 < a.cap; s0 += 32) {
+                    const int slot = s0 + lane;
+                    const int id = slot < a.cap ? mem[p * a.cap + slot] : -1;
+                    c += __popc(__ballot_sync(0xFFFFFFFFu, id >= a.sink && (int64_t)id < ws));
+                }
             }
             if (lane == 0) pick_kept[p] = c;
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int acc = 0;
-            for (int p = 0; p < 32; ++p) {
-                pick_off[p] = acc;
-                acc += pick_kept[p];
+        if (warp == 0) {
+            int c = pick_kept[lane], incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+                if (lane >= o) incl += y;
             }
-            list_len = acc < a.top_k ? acc : a.top_k;
+            pick_off[lane] = incl - c;
+            if (lane == 31) list_len = incl < a.top_k ? incl : a.top_k;
         }
         __syncthreads();
         const int nk = list_len;
-        for (int p = warp; p < 32; p += kDecWarps) {
+        for (int p = warp; p < kv; p += kDecWarps) {
             int base = pick_off[p];
             for (int s0 = 0; s0 < a.cap && base < nk; s0 += 32) {
                 const int slot = s0 + lane;
@@ -188,6 +204,7 @@ __global__ void __launch_bounds__(kDecThreads) fused_decode_kernel(const FusedDe
             else if (i < nwin + nsink) v = i - nwin;
             list[nk + i] = v;
         }
+        __syncthreads();
         if (threadIdx.x == 0) list_len = nk + nwin + nsink;
         __syncthreads();
         if (a.lists && h == 0 && split == 0) {
@@ -199,14 +216,31 @@ __global__ void __launch_bounds__(kDecThreads) fused_decode_kernel(const FusedDe
     // ------------------------------------------------------------------ D: split read
     const int len = list_len;
     const int lo = split * a.span, hi = min(lo + a.span, len);
+    const int nch = hi > lo ? (hi - lo + kDecChunk - 1) / kDecChunk : 0;
+    const T* kb = static_cast<const T*>(a.k) + (int64_t)h * 128;
+    const T* vb = static_cast<const T*>(a.v) + (int64_t)h * 128;
+    const int64_t rs = (int64_t)a.Hkv * 128;
+    // stage chunk c of the split's K and V rows into buffer c & 1 (16-byte copies, zero-fill
+    // for skipped ids); rows [kk][kv][128]
+    auto stage = [&](int c) {
+        T* dst = kvs + (c & 1) * kDecChunk * 2 * 128;
+        for (int t = threadIdx.x; t < kDecChunk * 2 * 16; t += kDecThreads) {
+            const int kk = t >> 5, kvsel = (t >> 4) & 1, c16 = t & 15;
+            const int j = lo + c * kDecChunk + kk;
+            const int id = j < hi ? list[j] : -1;
+            const bool ok = id >= 0 && id < a.Tk;
+            const T* src = (kvsel ? vb : kb) + (int64_t)(ok ? id : 0) * rs + c16 * 8;
+            cp_async16(smem_u32(dst + (kk * 2 + kvsel) * 128 + c16 * 8), src, ok ? 16u : 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (nch > 0) stage(0);
+    if (nch > 1) stage(1);
     const int sub = lane >> 4, dl = (lane & 15) * 8;  // half-warp = one key row, 8 dims per lane
     const T* qp = static_cast<const T*>(a.q) + ((int64_t)r * a.Hq + h * G) * 128 + dl;
     float qv[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g) load8<T>(qp + g * 128, qv[g]);
-    const T* kb = static_cast<const T*>(a.k) + (int64_t)h * 128 + dl;
-    const T* vb = static_cast<const T*>(a.v) + (int64_t)h * 128 + dl;
-    const int64_t rs = (int64_t)a.Hkv * 128;
     float m[G], l[G], o[G][8];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -215,48 +249,50 @@ __global__ void __launch_bounds__(kDecThreads) fused_decode_kernel(const FusedDe
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[g][e] = 0.0f;
     }
-    constexpr int UN = 4;  // key pairs per warp in flight
-    // the loop bound is warp-uniform (the shuffles below need all 32 lanes); a half-warp
-    // whose key falls past the split treats it as absent
-    for (int jw = lo + warp * 2; jw < hi; jw += kDecWarps * 2 * UN) {
-        float kx[UN][8], vx[UN][8];
-        bool live[UN];
-#pragma unroll
-        for (int i = 0; i < UN; ++i) {
-            const int j = jw + sub + i * kDecWarps * 2;
+    for (int c = 0; c < nch; ++c) {
+        if (c + 1 < nch)
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        const T* buf = kvs + (c & 1) * kDecChunk * 2 * 128;
+        // the loop bound is warp-uniform (the shuffles below need all 32 lanes)
+#pragma unroll 2
+        for (int i = 0; i < kDecChunk / (2 * kDecWarps); ++i) {
+            const int kk = i * 2 * kDecWarps + warp * 2 + sub;
+            const int j = lo + c * kDecChunk + kk;
             const int id = j < hi ? list[j] : -1;
-            live[i] = id >= 0 && id < a.Tk;
-            if (live[i]) {
-                load8<T>(kb + (int64_t)id * rs, kx[i]);
-                load8<T>(vb + (int64_t)id * rs, vx[i]);
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < UN; ++i) {
+            const bool live = id >= 0 && id < a.Tk;
+            float kx[8], vx[8];
+            load8<T>(buf + (kk * 2) * 128 + dl, kx);
+            load8<T>(buf + (kk * 2 + 1) * 128 + dl, vx);
             float s[G];
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 float acc = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc = fmaf(qv[g][e], live[i] ? kx[i][e] : 0.0f, acc);
+                for (int e = 0; e < 8; ++e) acc = fmaf(qv[g][e], kx[e], acc);
                 acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 8);
                 acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 4);
                 acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 2);
                 acc += __shfl_xor_sync(0xFFFFFFFFu, acc, 1);
                 s[g] = acc * a.scale_log2;
             }
-            if (!live[i]) continue;  // uniform within the half-warp
+            if (live) {  // uniform within the half-warp
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float mn = fmaxf(m[g], s[g]);
-                const float corr = exp2f(m[g] - mn);  // m = -inf first: 0
-                const float pw = exp2f(s[g] - mn);
-                l[g] = l[g] * corr + pw;
+                for (int g = 0; g < G; ++g) {
+                    const float mn = fmaxf(m[g], s[g]);
+                    const float corr = exp2f(m[g] - mn);  // m = -inf first: 0
+                    const float pw = exp2f(s[g] - mn);
+                    l[g] = l[g] * corr + pw;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) o[g][e] = fmaf(pw, vx[i][e], o[g][e] * corr);
-                m[g] = mn;
+                    for (int e = 0; e < 8; ++e) o[g][e] = fmaf(pw, vx[e], o[g][e] * corr);
+                    m[g] = mn;
+                }
             }
         }
+        __syncthreads();  // buffer c & 1 is free again
+        if (c + 2 < nch) stage(c + 2);
     }
     // merge the 16 half-warp states of the CTA through shared memory
     float* red_o = reinterpret_cast<float*>(dsm);                        // [16][G][128]
@@ -348,7 +384,8 @@ int occupancy_blocks(int smem) {
 DecodePlan plan_decode(int64_t R, int64_t Hkv, int64_t G, int64_t N, int64_t cap, int64_t width, int sms,
                        int per_sm) {
     DecodePlan p;
-    const int64_t list_smem = ((N * 8 + 15) / 16) * 16 + 32 * cap * 4 + width * 4;
+    const int64_t list_smem = ((N * 8 + 15) / 16) * 16 + ((32 * cap + width) * 4 + 15) / 16 * 16 +
+                              2 * kDecChunk * 2 * 128 * 2;
     const int64_t red_smem = 16 * G * 128 * 4 + 16 * G * 2 * 4;
     p.smem = (int)(list_smem > red_smem ? list_smem : red_smem);
     const int64_t resident = (int64_t)sms * (per_sm > 0 ? per_sm : 1);
@@ -399,7 +436,9 @@ int lsa_decode_fused(const void* index_queries, int64_t R, int64_t ldq, const vo
                      int32_t* lists, int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters,
                      int64_t n_counters, cudaStream_t stream) {
     if (R <= 0 || R > kDecMaxRows || D != 128 || Hkv <= 0 || Hq % Hkv || d <= 0 || d % 8 || ldq < d) return LSA_ERR_ARG;
-    if (top_p <= 0 || top_p > 32 || cap <= 0 || block <= 0 || top_k < 0 || window < 0 || sink < 0) return LSA_ERR_ARG;
+    if (top_p <= 0 || top_p > 32 || cap <= 0 || cap % 4 || block <= 0 || top_k < 0 || window < 0 || sink < 0)
+        return LSA_ERR_ARG;
+    if (((uintptr_t)members & 15) != 0) return LSA_ERR_ARG;
     if ((lists == nullptr) != (lengths == nullptr) || Tk > INT32_MAX) return LSA_ERR_ARG;
     if (dtype != kBF16 && dtype != kF16) return LSA_ERR_ARG;
     auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
