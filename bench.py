@@ -127,8 +127,9 @@ def _traffic_from_profile(name: str):
 # --------------------------------------------------------------------------- B200 arm
 
 
-def build_layers(dev, lsa):
-    """LAYERS independent caches: K/V, the decode row's q and index query, the Ward buckets."""
+def build_layers(dev, lsa, arms=False):
+    """LAYERS independent caches: K/V, the decode row's q and index query, the Ward buckets
+    (and with ``arms`` the node hierarchy and the positional buckets)."""
     import torch
 
     from lsa_b200.index_space import regroup_rows
@@ -144,10 +145,14 @@ def build_layers(dev, lsa):
         q = torch.randn(1, 1, HQ, DH, generator=gen, device=dev).to(torch.bfloat16)
         _, ik = regroup_rows(k[0], k[0])  # index keys (the query half of this call is unused)
         buckets = lsa.build_buckets_gpu(ik, pcfg)
+        # the other decode arms of the configuration: the tree over these buckets, and the
+        # positional block-sparse buckets
+        hierarchy = lsa.build_hierarchy_gpu(ik, buckets, pcfg) if arms else None
+        pbuckets = lsa.position_buckets(ik, pcfg) if arms else None
         del ik
         iq, _ = regroup_rows(q[0], k[0, -1:])
-        layers.append(dict(k=k, v=v, q=q, iq=iq.to(torch.bfloat16), buckets=buckets,
-                           pos=torch.tensor([T_CTX - 1], device=dev, dtype=torch.int32)))
+        layers.append(dict(k=k, v=v, q=q, iq=iq.to(torch.bfloat16), iq32=iq, buckets=buckets, hierarchy=hierarchy,
+                           pbuckets=pbuckets, pos=torch.tensor([T_CTX - 1], device=dev, dtype=torch.int32)))
     torch.cuda.synchronize(dev)
     return pcfg, layers
 
@@ -160,7 +165,7 @@ def run_b200(args, rank, world, dev):
 
     os.environ["LSA_SELECT_IMPL"] = "fused"
     scale = DH ** -0.5
-    pcfg, layers = build_layers(dev, lsa)
+    pcfg, layers = build_layers(dev, lsa, arms=not args.quick)
     stream = torch.cuda.Stream(dev)
 
     def select(L):
@@ -281,7 +286,7 @@ def run_b200(args, rank, world, dev):
                 outs.append(pipeline.decode_fused(qd[i], L["k"], L["v"], iq, L["pos"], L["buckets"], pcfg, scale))
         out_host.copy_(torch.stack(outs), non_blocking=True)
 
-    e2e_ms, us_dense = float("nan"), float("nan")
+    e2e_ms, us_dense, us_tree, us_positional = float("nan"), float("nan"), float("nan"), float("nan")
     if not args.quick:
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -309,6 +314,23 @@ def run_b200(args, rank, world, dev):
             for L in layers:
                 lsa.dense_read(L["q"], L["k"], L["v"], scale)
         us_dense = timed(dense_graph, reps=2) / LAYERS * 1e3
+
+        # the configuration's other arms on the same rotation: D-LSA Tree and positional
+        def arm_ms(select_fn):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                for L in layers:
+                    ls, ln = select_fn(L)
+                    read(L, ls, ln)
+                stream.synchronize()
+            with torch.cuda.graph(gr, stream=stream):
+                for L in layers:
+                    ls, ln = select_fn(L)
+                    read(L, ls, ln)
+            return timed(gr, reps=2) / LAYERS * 1e3
+
+        us_tree = arm_ms(lambda L: lsa.tree_select(L["iq32"], L["pos"], L["buckets"], L["hierarchy"], pcfg))
+        us_positional = arm_ms(lambda L: pipeline.positional_select(L["pos"], L["pbuckets"], pcfg))
 
     hbm, tflops, peak_kind = _load_peaks()
     read_gbs = read_bytes_per_launch / (us_read * 1e-6) / 1e9
@@ -339,6 +361,9 @@ def run_b200(args, rank, world, dev):
         "read_roofline": {"kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
                           "frac": round(read_gbs / hbm, 4)},
         "dense_us_per_decode": round(us_dense, 3),
+        "arms_us_per_decode": None if us_tree != us_tree else {
+            "flat": round(ms_split / args.steps / LAYERS * 1e3, 3), "tree": round(us_tree, 3),
+            "positional": round(us_positional, 3), "dense": round(us_dense, 3)},
         "speedup_vs_dense_decode": (round(us_dense / (ms_per_step / LAYERS * 1e3), 3)
                                     if us_dense == us_dense else None),
         "bytes_per_step": step_bytes, "keys_read_per_step": n_ids,

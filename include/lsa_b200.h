@@ -122,6 +122,14 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
                      int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                      int64_t max_position, cudaStream_t stream);
 
+/* cfg 2's positional block-sparse arm (pipeline.py:378-403 builds its buckets; the static
+ * pattern is this build's definition): per row, of the v visible buckets the first `first`,
+ * the last `last` and top_p - first - last strided in between (first + floor(i * (v - first
+ * - last) / (top_p - first - last))), ascending, unique, -1 padded; every visible bucket
+ * when v <= top_p. picks [R, top_p] int32, then lsa_expand_in_order. */
+int lsa_positional_picks(const int32_t* positions, int64_t R, int64_t block, int64_t bpb, int64_t rows, int64_t top_p,
+                         int64_t first, int64_t last, int32_t* picks, cudaStream_t stream);
+
 /* Batched decode (one query row per sequence, sequences of different lengths): the fused
  * selection of flat_select (pipeline.py:274-316) for every row in one launch, row r reading
  * its own sequence's buckets = rows [table_off[r], table_off[r] + table_rows[r]) of the

@@ -86,6 +86,40 @@ __global__ void unpack_kernel(const int64_t* __restrict__ keys, int64_t n, int32
     if (i < n) ids[i] = key_bucket(keys[i]);
 }
 
+// ------------------------------------------------------------------ positional arm
+
+// The positional decode arm's static picks: of a row's visible buckets v = min(rows,
+// pos / block * bpb), the first `first`, the last `last`, and top_p - first - last strided
+// ones in between (bucket first + floor(i * (v - first - last) / n_mid)), ascending and
+// unique, -1 padded; v <= top_p: every visible bucket.
+__global__ void positional_picks_kernel(const int32_t* __restrict__ positions, int64_t R, int64_t block, int64_t bpb,
+                                        int64_t rows, int top_p, int first, int last, int32_t* __restrict__ picks) {
+    const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    int64_t v = (int64_t)positions[r] / block * bpb;
+    if (v > rows) v = rows;
+    if (v < 0) v = 0;
+    int32_t* out = picks + r * top_p;
+    int n = 0;
+    if (v <= top_p) {
+        for (int64_t b = 0; b < v; ++b) out[n++] = (int32_t)b;
+    } else {
+        const int mid = top_p - first - last;
+        const int64_t span = v - first - last;
+        for (int i = 0; i < first; ++i) out[n++] = i;
+        int64_t prev = first - 1;
+        for (int i = 0; i < mid; ++i) {
+            const int64_t b = first + (int64_t)i * span / mid;
+            if (b > prev && b < v - last) {
+                out[n++] = (int32_t)b;
+                prev = b;
+            }
+        }
+        for (int i = 0; i < last; ++i) out[n++] = (int32_t)(v - last + i);
+    }
+    for (; n < top_p; ++n) out[n] = -1;
+}
+
 // ------------------------------------------------------------------ top-k
 
 // Loader interface: key(n) for n < N. Sorted top-k of N keys into out[0..k) (EMPTY past N).
@@ -829,6 +863,16 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
 extern "C" {
 
 int64_t lsa_select_batched_scratch(int64_t R, int64_t max_rows) { return lsa_select_fused_scratch(R, max_rows); }
+
+int lsa_positional_picks(const int32_t* positions, int64_t R, int64_t block, int64_t bpb, int64_t rows, int64_t top_p,
+                         int64_t first, int64_t last, int32_t* picks, cudaStream_t stream) {
+    if (R < 0 || block <= 0 || top_p <= 0 || first < 0 || last < 0 || first + last > top_p) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    positional_picks_kernel<<<(unsigned)((R + 127) / 128), 128, 0, stream>>>(positions, R, block, bpb, rows,
+                                                                             (int)top_p, (int)first, (int)last, picks);
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
 
 int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
                        int64_t d, const int64_t* table_off, const int32_t* table_rows, int64_t max_rows,

@@ -53,6 +53,7 @@ SIGNATURES = {
     "lsa_pair_to_size_workspace": (_I, [_I, _I, _I]),
     "lsa_pair_to_size": (_INT, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P]),
     "lsa_sparse_read_noalloc": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _I, _P]),
+    "lsa_positional_picks": (_INT, [_P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_select_batched_scratch": (_I, [_I, _I]),
     "lsa_select_batched": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _P, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P,
                                   _P, _P, _I, _P, _I, _I, _P]),

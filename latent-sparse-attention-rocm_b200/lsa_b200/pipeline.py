@@ -167,6 +167,25 @@ def position_buckets(index_keys: torch.Tensor, config: PortConfig) -> Buckets:
     return Buckets(cb, members, sizes, centroids_f32=cf, key_sums=sums)
 
 
+def positional_picks(positions: torch.Tensor, buckets: Buckets, config: PortConfig, first: int = 4,
+                     last: int = 4) -> torch.Tensor:
+    """cfg 2's positional arm: first/last visible buckets plus strided ones, [R, top_p] int32."""
+    require_cuda(positions, what="positional_picks")
+    pos = positions.to(torch.int32).contiguous()
+    picks = torch.empty(pos.shape[0], config.top_p, dtype=torch.int32, device=pos.device)
+    check(lib().lsa_positional_picks(ptr(pos), pos.shape[0], config.cluster_block_size, config.block_bucket_count,
+                                     buckets.rows, config.top_p, first, last, ptr(picks), stream_of(pos)),
+          "positional_picks")
+    return picks
+
+
+def positional_select(positions, buckets: Buckets, config: PortConfig, top_k=None, first: int = 4, last: int = 4):
+    """The positional decode arm over ``position_buckets``: static picks, the same expansion."""
+    top_k = config.top_k if top_k is None else top_k
+    picks = positional_picks(positions, buckets, config, first, last)
+    return expand_in_order(picks, buckets.members, positions, config.window_size, config.sink_size, top_k)
+
+
 def _normalize(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(x)
     if x.shape[0]:

@@ -220,3 +220,15 @@ def test_expand_matches_reference_walk(oracle, positions, window, sink, top_k, t
     got_l, got_n = oracle.expand(picked, members, pos, window, sink, top_k)
     want_l, want_n = _walk_reference_style(picked, members, pos, window, sink, top_k, tile)
     assert (got_l == want_l).all() and (got_n == want_n).all()
+
+
+def test_positional_picks_pattern(oracle):
+    """The static positional arm: all visible buckets when few, else first 4, last 4 and
+    24 strided between them, ascending and unique."""
+    cfg = oracle.Config(cluster_block_size=512, bucket_size=64, top_p=32)
+    p = oracle.positional_picks([100, 2047, 3000, 32767], 512, cfg)
+    assert (p[0] == -1).all()  # nothing closed yet
+    assert (p[1][:24] == np.arange(24)).all() and (p[1][24:] == -1).all()  # 24 visible: all of them
+    for row, v in ((p[2], 40), (p[3], 504)):
+        assert row.size == 32 and (np.diff(row) > 0).all() and (row >= 0).all()
+        assert list(row[:4]) == [0, 1, 2, 3] and list(row[-4:]) == [v - 4, v - 3, v - 2, v - 1]
