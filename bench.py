@@ -287,6 +287,7 @@ def run_b200(args, rank, world, dev):
         out_host.copy_(torch.stack(outs), non_blocking=True)
 
     e2e_ms, us_dense, us_tree, us_positional = float("nan"), float("nan"), float("nan"), float("nan")
+    ms_batch = float("nan")
     if not args.quick:
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -332,6 +333,26 @@ def run_b200(args, rank, world, dev):
         us_tree = arm_ms(lambda L: lsa.tree_select(L["iq32"], L["pos"], L["buckets"], L["hierarchy"], pcfg))
         us_positional = arm_ms(lambda L: pipeline.positional_select(L["pos"], L["pbuckets"], pcfg))
 
+        # the same LAYERS caches decoded as ONE batch of LAYERS sequences (one batched select
+        # launch + one batched read launch): the bandwidth view of this decode
+        from lsa_b200 import batched
+
+        kb = torch.cat([L["k"] for L in layers])
+        vb = torch.cat([L["v"] for L in layers])
+        qb = torch.cat([L["q"] for L in layers])
+        iqb = torch.cat([L["iq"] for L in layers])
+        posb = torch.cat([L["pos"] for L in layers])
+        bb = batched.concat_buckets([L["buckets"] for L in layers])
+        bgraph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            batched.batched_decode(qb, kb, vb, iqb, posb, bb, pcfg, scale)
+            stream.synchronize()
+        with torch.cuda.graph(bgraph, stream=stream):
+            for _ in range(args.steps):
+                batched.batched_decode(qb, kb, vb, iqb, posb, bb, pcfg, scale)
+        ms_batch = timed(bgraph) / args.steps
+        del kb, vb, bgraph
+
     hbm, tflops, peak_kind = _load_peaks()
     read_gbs = read_bytes_per_launch / (us_read * 1e-6) / 1e9
     fused_impl = args.decode_impl != "split"
@@ -361,6 +382,10 @@ def run_b200(args, rank, world, dev):
         "read_roofline": {"kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
                           "frac": round(read_gbs / hbm, 4)},
         "dense_us_per_decode": round(us_dense, 3),
+        "batch_decode": None if ms_batch != ms_batch else {
+            "sequences": LAYERS, "us_per_batch": round(ms_batch * 1e3, 2), "gbs": round(step_bytes / (ms_batch * 1e-3) / 1e9, 1),
+            "hbm_frac": round(step_bytes / (ms_batch * 1e-3) / 1e9 / hbm, 4),
+            "note": "the LAYERS caches decoded as one batch (batched select + batched read)"},
         "arms_us_per_decode": None if us_tree != us_tree else {
             "flat": round(ms_split / args.steps / LAYERS * 1e3, 3), "tree": round(us_tree, 3),
             "positional": round(us_positional, 3), "dense": round(us_dense, 3)},
