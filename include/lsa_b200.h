@@ -115,7 +115,10 @@ int64_t lsa_select_fused_scratch(int64_t R, int64_t N);
 
 /* flat_select with LSA_SELECT_IMPL=fused (pipeline.py:274-316): ONE launch from index queries
  * to read lists - scoring over many CTAs, the last CTA of a row sorts and expands.
- * counters: R int32. max_position < 0: size the grid for every column. */
+ * counters: R int32 tickets (zero at rest), and with R + 1 the status word counters[R]:
+ * rows wider than one cluster with bf16 centroids, top_p <= 128 and cap % 4 == 0 then take
+ * the persistent streaming kernel (TMA bulk copies of the centroid rows), whose bounded
+ * waits record LSA_ERR_TIMEOUT there. max_position < 0: size the grid for every column. */
 int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
                      int64_t N, int64_t d, const int32_t* positions, int64_t block, int64_t bpb, const int32_t* members,
                      int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
@@ -136,7 +139,8 @@ int lsa_positional_picks(const int32_t* positions, int64_t R, int64_t block, int
  * concatenated centroid [sum rows, d] and member [sum rows, cap] tables (member ids are
  * positions within the row's sequence). max_rows = the largest table_rows[r] (the scratch
  * key stride). Each row's result equals flat_select on its own sequence's buckets. The
- * reference has no batched select (its gates build per sequence, gates.py:59). */
+ * reference has no batched select (its gates build per sequence, gates.py:59). Counters
+ * as lsa_select_fused (R tickets, + 1 status word to allow the streaming kernel). */
 int64_t lsa_select_batched_scratch(int64_t R, int64_t max_rows);
 int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,
                        int64_t d, const int64_t* table_off, const int32_t* table_rows, int64_t max_rows,

@@ -153,6 +153,39 @@ __host__ __device__ __forceinline__ int next_pow2(int x) {
     return p;
 }
 
+// Exclusive scan of one int per thread over a group of NT threads (tid in [0, NT), NT a
+// multiple of 32, at most 1024) that share the barrier `sync`. Returns the exclusive prefix;
+// *total receives the group sum. Uses 33 ints of smem.
+template <int NT, typename Sync>
+__device__ __forceinline__ int group_exclusive_scan(int v, int* smem, int* total, int tid, Sync sync) {
+    constexpr int NWARPS = NT / 32;
+    const int lane = tid & 31, warp = tid >> 5;
+    int x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        int y = __shfl_up_sync(0xFFFFFFFFu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) smem[warp] = x;
+    sync();
+    if (warp == 0) {
+        int w = lane < NWARPS ? smem[lane] : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            int y = __shfl_up_sync(0xFFFFFFFFu, w, off);
+            if (lane >= off) w += y;
+        }
+        if (lane < NWARPS) smem[lane] = w;  // inclusive prefix of warp sums
+        if (lane == NWARPS - 1) smem[32] = w;
+    }
+    sync();
+    int before = warp > 0 ? smem[warp - 1] : 0;
+    int res = before + x - v;
+    *total = smem[32];
+    sync();
+    return res;
+}
+
 // Block-wide exclusive scan of one int per thread (blockDim.x <= 1024, multiple of 32).
 // Returns the exclusive prefix; *total receives the block sum. Uses 33 ints of smem.
 __device__ __forceinline__ int block_exclusive_scan(int v, int* smem, int* total) {

@@ -11,8 +11,9 @@
 // all G query heads of the KV head, so each gathered K/V row crosses HBM once per group.
 // The CTA's ids are fetched in stages (128 ids for 16-bit types): every warp issues one
 // cp.async.bulk (TMA bulk copy) per listed K row and V row of its 16 slots straight into
-// shared memory, completion counted by an mbarrier (one expect_tx arrival per warp), two
-// stages in flight; the id and length loads overlap (no dependent round trip). A lane holds
+// shared memory, completion counted by an mbarrier (one expect_tx arrival per warp), three
+// stages in flight; the ids of the next stage to issue load while the current stage waits
+// and computes, so no id round trip sits between a freed buffer and its refill. A lane holds
 // 8 elements (one 16-byte vector) of a row; 16 lanes cover a Dh = 128 row.
 // Split partials (m, l, o) merge three ways:
 //   * 1 split: the CTA writes the output;
@@ -28,6 +29,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "umma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -42,20 +44,7 @@ template <typename T>
 struct StageIds {
     static constexpr int value = sizeof(T) == 4 ? 64 : 128;
 };
-
-__device__ __forceinline__ void mbar_expect_tx_arrive(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
+constexpr int kReadStages = 3;  // K/V stages in flight (ring of shared-memory buffers)
 
 // Four 8x8 b16 matrices from shared memory (lane l addresses row l & 7 of matrix l >> 3).
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -164,11 +153,12 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     constexpr int STAGE_BYTES = STAGE * ROWS * (int)sizeof(T);
     constexpr int IDW = STAGE / NW;     // id slots a warp issues per stage
     static_assert(2 * IDW <= 32, "a warp issues the K and V rows of its slots in one pass");
+    constexpr int NST = kReadStages;
     extern __shared__ __align__(128) unsigned char smem[];
-    T* sK = reinterpret_cast<T*>(smem);                    // [2][STAGE][D]
-    T* sV = reinterpret_cast<T*>(smem + 2 * STAGE_BYTES);  // [2][STAGE][D]
-    __shared__ __align__(8) uint64_t bars[2];
-    __shared__ unsigned char sflag[2 * STAGE];              // slot listed and in range
+    T* sK = reinterpret_cast<T*>(smem);                      // [NST][STAGE][D]
+    T* sV = reinterpret_cast<T*>(smem + NST * STAGE_BYTES);  // [NST][STAGE][D]
+    __shared__ __align__(8) uint64_t bars[NST];
+    __shared__ unsigned char sflag[NST * STAGE];              // slot listed and in range
     __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -182,8 +172,8 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     const int G = a.G;
 
     if (tid == 0) {
-        mbar_init(&bars[0], NW);  // one expect_tx arrival per warp per stage
-        mbar_init(&bars[1], NW);
+#pragma unroll
+        for (int i = 0; i < NST; ++i) mbar_init(&bars[i], NW);  // one expect_tx arrival per warp per stage
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
@@ -204,7 +194,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
         int at = s0 + stage * STAGE + my_slot;
         return (issuer && at < s0 + a.span && at < a.width) ? idrow[at] - a.id_base : -1;
     };
-    int id0 = load_id(0), id1 = load_id(1);
+    int id_first[NST];
+#pragma unroll
+    for (int i = 0; i < NST; ++i) id_first[i] = load_id(i);
+    int id_next = load_id(NST);  // the stage issued when buffer 0 frees
     int len = a.lengths[row];
     len = len < 0 ? 0 : (len > a.width ? a.width : len);
     const int s1 = min(s0 + a.span, len);
@@ -212,11 +205,11 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     const int n_stages = (n_ids + STAGE - 1) / STAGE;
 
     auto issue = [&](int stage, int id) {
-        int buf = stage & 1;
+        int buf = stage % NST;
         int at = s0 + stage * STAGE + my_slot;
         bool ok = issuer && at < s1 && id >= 0 && id < a.Tk;
         uint32_t n = __popc(__ballot_sync(0xFFFFFFFFu, ok));
-        if (lane == 0) mbar_expect_tx_arrive(&bars[buf], n * ROWB);
+        if (lane == 0) mbar_arrive_expect_tx(&bars[buf], n * ROWB);
         if (issuer && !is_v) sflag[buf * STAGE + my_slot] = ok ? 1 : 0;
         __syncwarp();
         if (ok) {
@@ -226,9 +219,15 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
         }
     };
 
-    if (n_stages > 0) issue(0, id0);
-    if (n_stages > 1) issue(1, id1);
+#pragma unroll
+    for (int i = 0; i < NST; ++i)
+        if (i < n_stages) issue(i, id_first[i]);
     __syncthreads();  // slot flags visible to every group
+    // on an expired wait: thread 0 waits (bounded) for every stage still in flight
+    auto drain = [&](int st) {
+        if (tid == 0)
+            for (int s2 = st; s2 < n_stages && s2 < st + NST; ++s2) mbar_wait_bounded(&bars[s2 % NST], (s2 / NST) & 1);
+    };
 
     bool failed = false;
     float* red = reinterpret_cast<float*>(smem);  // [NGE][GMAX][D] group partials (after the loop)
@@ -255,10 +254,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
         for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
         float mrow = kNegBig, lrow = 0.0f;  // row gq (this thread's share of l; quad-summed at the end)
         for (int st = 0; st < n_stages; ++st) {
-            int buf = st & 1;
-            bool ok = mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+            int buf = st % NST;
+            bool ok = mbar_wait_bounded(&bars[buf], (st / NST) & 1);
             if (__syncthreads_or(!ok)) {  // block-uniform: every thread leaves together
-                if (tid == 0) mbar_wait_bounded(&bars[buf], (st >> 1) & 1);  // copies in flight
+                drain(st);  // copies in flight
                 __syncthreads();
                 failed = true;
                 break;
@@ -272,6 +271,9 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                 float sc[2][4];
 #pragma unroll
                 for (int j = 0; j < 2; ++j) {
+                    // two accumulator chains per key tile (even / odd k16 blocks), summed after:
+                    // half the dependent MMA latency of one chain
+                    float s2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                     sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
 #pragma unroll
                     for (int q4 = 0; q4 < DC / 2; ++q4) {  // 4 dim blocks of 8 per ldmatrix.x4
@@ -279,8 +281,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                         uint32_t addr = kaddr + ((8 * j + (lane & 7)) * ROWS + (4 * q4 + (lane >> 3)) * 8) * 2;
                         ldsm_x4(addr, b0, b1, b2, b3);
                         mma16816<T>(sc[j], qa[2 * q4][0], 0u, qa[2 * q4][1], 0u, b0, b1);
-                        mma16816<T>(sc[j], qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
+                        mma16816<T>(s2, qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
                     }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) sc[j][e] += s2[e];
                 }
                 // scores of row gq for keys 8j + 2tq + {0, 1}; unlisted slots never count
                 float sv[4];
@@ -329,7 +333,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                 }
             }
             __syncthreads();  // every warp is done with this buffer
-            if (st + 2 < n_stages) issue(st + 2, load_id(st + 2));
+            if (st + NST < n_stages) {
+                issue(st + NST, id_next);
+                id_next = load_id(st + NST + 1);
+            }
         }
         if (!failed) {
             lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 1);
@@ -370,10 +377,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
             for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
         }
         for (int st = 0; st < n_stages; ++st) {
-            int buf = st & 1;
-            bool ok = mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+            int buf = st % NST;
+            bool ok = mbar_wait_bounded(&bars[buf], (st / NST) & 1);
             if (__syncthreads_or(!ok)) {
-                if (tid == 0) mbar_wait_bounded(&bars[buf], (st >> 1) & 1);
+                drain(st);
                 __syncthreads();
                 failed = true;
                 break;
@@ -432,7 +439,10 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                 }
             }
             __syncthreads();
-            if (st + 2 < n_stages) issue(st + 2, load_id(st + 2));
+            if (st + NST < n_stages) {
+                issue(st + NST, id_next);
+                id_next = load_id(st + NST + 1);
+            }
         }
         if (!failed) {
 #pragma unroll
@@ -582,7 +592,7 @@ static constexpr int read_smem_bytes() {
     constexpr int NG = (kReadThreads / 32) * (32 / (D / 8));
     constexpr int NGE = MMA ? kReadThreads / 32 : NG;
     constexpr int ROWS = MMA ? D + 8 : D;
-    constexpr int stage_bytes = 4 * STAGE * ROWS * (int)sizeof(T);
+    constexpr int stage_bytes = 2 * kReadStages * STAGE * ROWS * (int)sizeof(T);
     constexpr int red_bytes = (NGE * GMAX * D + NGE * GMAX * 2 + GMAX * D + GMAX * 2) * 4;
     return stage_bytes > red_bytes ? stage_bytes : red_bytes;
 }

@@ -16,6 +16,7 @@
 
 #include "common.cuh"
 #include "topk.cuh"
+#include "umma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -337,15 +338,88 @@ __device__ __forceinline__ int64_t block_bitonic_desc_regs(int64_t x, int64_t* x
     return x;
 }
 
+// The rank-order walk over staged member slots mem[0, total) (slot p * cap + m holds member
+// m of the p-th pick; -1 and ids outside [sink, ws) are skipped): one scan over all slots
+// gives every thread its output offset, kept ids go out in slot order up to top_k, then the
+// window [ws, pos] and the sinks [0, min(sink, ws)). Run by NT threads (tid in [0, NT)) that
+// share the barrier `sync`; mem must be 16-byte aligned.
+template <int NT, typename Sync>
+__device__ void expand_walk(const int* mem, int total, int64_t pos, int window, int sink, int top_k,
+                            int32_t* __restrict__ out, int width, int32_t* length_out, int* scan_smem, int tid,
+                            Sync sync, int* gather = nullptr) {
+    // gather (top_k ints of shared memory, optional): kept ids land there first and leave in
+    // one coalesced copy instead of scattered 4-byte stores per thread
+    int32_t* dst = gather ? gather : out;
+    int64_t ws = pos + 1 - window;
+    if (ws < 0) ws = 0;
+    auto keep = [&](int v) { return v >= 0 && v >= sink && (int64_t)v < ws; };
+    const int spt = (total + NT - 1) / NT;
+    const int first = tid * spt;
+    const bool vec = spt % 4 == 0 && first + spt <= total;  // contiguous 16-byte reads of this thread's slots
+    int cnt = 0;
+    if (vec) {
+        for (int i = 0; i < spt; i += 4) {
+            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
+            cnt += keep(v.x) + keep(v.y) + keep(v.z) + keep(v.w);
+        }
+    } else {
+        for (int i = 0; i < spt; ++i) {
+            int s = first + i;
+            cnt += (s < total && keep(mem[s]));
+        }
+    }
+    int filled;
+    int at = group_exclusive_scan<NT>(cnt, scan_smem, &filled, tid, sync);
+    if (vec) {
+        for (int i = 0; i < spt && at < top_k; i += 4) {
+            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
+            const int e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (keep(e[u])) {
+                    if (at < top_k) dst[at] = e[u];
+                    ++at;
+                }
+            }
+        }
+    } else {
+        for (int i = 0; i < spt && at < top_k; ++i) {
+            int s = first + i;
+            if (s < total && keep(mem[s])) {
+                dst[at] = mem[s];
+                ++at;
+            }
+        }
+    }
+    if (filled > top_k) filled = top_k;
+    if (gather) {
+        sync();
+        for (int i = tid; i < filled; i += NT) out[i] = gather[i];
+    }
+    int nwin = (int)(pos - ws + 1);
+    if (nwin < 0) nwin = 0;
+    int nsink = (int)(sink < ws ? sink : ws);
+    for (int i = tid; i < width - filled; i += NT) {
+        int j = filled + i, v = -1;
+        if (i < nwin) v = (int)(ws + i);
+        else if (i < nwin + nsink) v = i - nwin;
+        out[j] = v;
+    }
+    if (tid == 0) *length_out = filled + nwin + nsink;
+}
+
+struct BlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
 // The walk of expand_row with every picked bucket's member row staged in shared memory
-// first (one memory round trip), then one block scan over all (pick, member) slots.
-// Requires P * cap <= kMemberPrefetch; mem holds that many int32.
+// first (one memory round trip), then expand_walk over all (pick, member) slots. A block of
+// kFusedThreads threads. Requires P * cap <= kMemberPrefetch; mem (16-byte aligned) holds
+// that many int32.
 __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t* __restrict__ members,
                                       int64_t member_rows, int cap, int64_t pos, int window, int sink, int top_k,
                                       int32_t* __restrict__ out, int width, int32_t* length_out, int* scan_smem,
                                       int* mem) {
-    int64_t ws = pos + 1 - window;
-    if (ws < 0) ws = 0;
     const int total = P * cap;
     // addresses first, then every member load of this thread in flight together, then the
     // stores: one memory round trip for the whole staging
@@ -353,7 +427,7 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     const int32_t* src[kMaxPer];
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
-        int s = threadIdx.x + i * blockDim.x;
+        int s = threadIdx.x + i * kFusedThreads;
         src[i] = nullptr;
         if (s < total) {
             int p = s / cap, m = s - p * cap;
@@ -366,61 +440,12 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     for (int i = 0; i < kMaxPer; ++i) vals[i] = src[i] ? __ldg(src[i]) : -1;
 #pragma unroll
     for (int i = 0; i < kMaxPer; ++i) {
-        int s = threadIdx.x + i * blockDim.x;
-        if (s < total) {
-            int v = vals[i];
-            mem[s] = (v < sink || v >= ws) ? -1 : v;
-        }
+        int s = threadIdx.x + i * kFusedThreads;
+        if (s < total) mem[s] = vals[i];
     }
     __syncthreads();
-    const int spt = (total + blockDim.x - 1) / blockDim.x;
-    const int first = threadIdx.x * spt;
-    int cnt = 0;
-    if (spt % 4 == 0 && first + spt <= total) {  // contiguous 16-byte reads of this thread's slots
-        for (int i = 0; i < spt; i += 4) {
-            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
-            cnt += (v.x >= 0) + (v.y >= 0) + (v.z >= 0) + (v.w >= 0);
-        }
-    } else {
-        for (int i = 0; i < spt; ++i) {
-            int s = first + i;
-            cnt += (s < total && mem[s] >= 0);
-        }
-    }
-    int filled;
-    int at = block_exclusive_scan(cnt, scan_smem, &filled);
-    if (spt % 4 == 0 && first + spt <= total) {
-        for (int i = 0; i < spt && at < top_k; i += 4) {
-            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
-            const int e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (e[u] >= 0) {
-                    if (at < top_k) out[at] = e[u];
-                    ++at;
-                }
-            }
-        }
-    } else {
-        for (int i = 0; i < spt && at < top_k; ++i) {
-            int s = first + i;
-            if (s < total && mem[s] >= 0) {
-                out[at] = mem[s];
-                ++at;
-            }
-        }
-    }
-    if (filled > top_k) filled = top_k;
-    int nwin = (int)(pos - ws + 1);
-    if (nwin < 0) nwin = 0;
-    int nsink = (int)(sink < ws ? sink : ws);
-    for (int i = threadIdx.x; i < width - filled; i += blockDim.x) {
-        int j = filled + i, v = -1;
-        if (i < nwin) v = (int)(ws + i);
-        else if (i < nwin + nsink) v = i - nwin;
-        out[j] = v;
-    }
-    if (threadIdx.x == 0) *length_out = filled + nwin + nsink;
+    expand_walk<kFusedThreads>(mem, total, pos, window, sink, top_k, out, width, length_out, scan_smem,
+                               (int)threadIdx.x, BlockSync{});
 }
 
 // One launch from index queries to read lists. grid = (chunks, R), block = 512: every
@@ -520,7 +545,7 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     }
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
-        int* mem = reinterpret_cast<int*>(sbuf + k);
+        int* mem = reinterpret_cast<int*>(sbuf + ((k + 1) & ~1));  // 16-byte aligned
         expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
                               lengths + r, scan_smem, mem);
     } else {
@@ -613,7 +638,7 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     }
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
-        int* mem = reinterpret_cast<int*>(sbuf + max(k, 32));
+        int* mem = reinterpret_cast<int*>(sbuf + ((max(k, 32) + 1) & ~1));  // 16-byte aligned
         expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
                               lengths + r, scan_smem, mem);
     } else {
@@ -624,6 +649,219 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
 }
 
 // ------------------------------------------------------------------ host helpers
+
+// ------------------------------------------------------------------ streaming select
+
+// Rows wider than one cluster (batched decode over long sequences, top_p <= 128) take two
+// launches. (1) select_stream_kernel, a persistent grid, streams the centroid tables
+// through shared memory with TMA bulk copies while scoring warps consume them, so HBM sees
+// one continuous stream per SM:
+//   * work items: 128 visible columns of one row; CTA b takes items b, b + grid, ... in
+//     row order;
+//   * one producer warp (lane 0) copies 32 KB stages (contiguous centroid rows) into a ring
+//     of kStreamStages buffers (full/empty mbarriers, bounded waits) and posts each stage's
+//     (row, first column, columns) beside it;
+//   * kStreamWarps scoring warps score the staged columns (canonical cdot, the row's query
+//     in registers) into packed keys in global scratch [R, N].
+// (2) select_finish_kernel, one CTA per row (programmatic dependent launch): the row's top
+// K = 32 KW keys by warp-list sorts and a merge tree, the picked member rows staged with
+// cp.async, and the expansion walk with its output gathered in shared memory.
+// Counters: counters[R] is the status word (LSA_ERR_TIMEOUT after an expired wait).
+constexpr int kStreamWarps = 8;
+constexpr int kStreamThreads = 32 * (kStreamWarps + 1);
+constexpr int kStreamStages = 3;
+constexpr int kStreamStageBytes = 32768;
+constexpr int kStreamItemCols = 128;
+constexpr int kStreamMaxRows = 256;
+constexpr int kFinishMaxTopK = 16384;  // read-list slots gathered in shared memory
+
+struct StreamStage {
+    int row;  // < 0: no more items for this CTA
+    int col0, ncols;
+};
+
+__device__ __forceinline__ int64_t stream_visible(const RowPos& rp, int r, int64_t N, int64_t block, int64_t bpb) {
+    const int64_t Nr = rp.rows(r, N);
+    int64_t cnt = rp.count_pos(r) / block * bpb;
+    if (cnt > Nr) cnt = Nr;
+    return cnt < 0 ? 0 : cnt;
+}
+
+template <typename TQ, int CHUNKS>
+__global__ void __launch_bounds__(kStreamThreads, 2) select_stream_kernel(
+    const TQ* __restrict__ q, int64_t ldq, const __nv_bfloat16* __restrict__ c, int64_t N, int d, RowPos rp,
+    int64_t block, int64_t bpb, int R, int64_t* __restrict__ ws_keys, int32_t* __restrict__ status) {
+    constexpr int NS = kStreamStages;
+    extern __shared__ __align__(128) unsigned char stage_buf[];  // [NS][32 KB]
+    __shared__ __align__(8) uint64_t full[NS], empty[NS];
+    __shared__ StreamStage meta[NS];
+    __shared__ int item_start[kStreamMaxRows + 1];
+    __shared__ int row_count[kStreamMaxRows];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], kStreamWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    pdl_wait();
+    pdl_trigger();
+    // visible columns of every row and the first item of every row (rows over the lanes)
+    if (warp == 0) {
+        constexpr int PER = kStreamMaxRows / 32;
+        int n_items[PER];
+        int mine = 0;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int r = lane * PER + i;
+            n_items[i] = 0;
+            if (r < R) {
+                const int64_t cnt = stream_visible(rp, r, N, block, bpb);
+                row_count[r] = (int)cnt;
+                n_items[i] = (int)((cnt + kStreamItemCols - 1) / kStreamItemCols);
+            }
+            mine += n_items[i];
+        }
+        int incl = mine;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            int y = __shfl_up_sync(0xFFFFFFFFu, incl, off);
+            if (lane >= off) incl += y;
+        }
+        int at = incl - mine;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+            const int r = lane * PER + i;
+            if (r < R) item_start[r] = at;
+            at += n_items[i];
+        }
+        if (lane == 31) item_start[kStreamMaxRows] = incl;
+    }
+    __syncthreads();
+    const int total_items = item_start[kStreamMaxRows];
+
+    if (warp == kStreamWarps) {  // producer
+        if (lane == 0) {
+            const int cps = kStreamStageBytes / (d * 2);  // columns per stage
+            int s = 0;
+            bool ok = true;
+            for (int it = blockIdx.x;; it += gridDim.x) {
+                const bool stop = it >= total_items;
+                int r = 0, col0 = 0, col1 = 0;
+                if (!stop) {  // the last row whose first item is at or before it (empty rows share it)
+                    int lo = 0, hi = R - 1;
+                    while (lo < hi) {
+                        int mid = (lo + hi + 1) >> 1;
+                        if (item_start[mid] <= it) lo = mid;
+                        else hi = mid - 1;
+                    }
+                    r = lo;
+                    col0 = (it - item_start[r]) * kStreamItemCols;
+                    col1 = min(col0 + kStreamItemCols, row_count[r]);
+                }
+                for (int c0 = col0;; c0 += cps) {  // a stop posts one stage with row -1
+                    const int slot = s % NS;
+                    if (!mbar_wait_bounded(&empty[slot], ((s / NS) & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const int n = stop ? 0 : min(cps, col1 - c0);
+                    meta[slot] = StreamStage{stop ? -1 : r, c0, n};
+                    if (n > 0) {
+                        mbar_arrive_expect_tx(&full[slot], (uint32_t)(n * d * 2));
+                        bulk_g2s(stage_buf + slot * kStreamStageBytes, c + (rp.off(r) + c0) * d, (uint32_t)(n * d * 2),
+                                 &full[slot]);
+                    } else {
+                        mbar_arrive(&full[slot]);
+                    }
+                    ++s;
+                    if (stop || c0 + cps >= col1) break;
+                }
+                if (stop || !ok) break;
+            }
+            if (!ok) {  // the scoring warps stopped consuming: wait (bounded) for copies in flight
+                atomicExch(status, LSA_ERR_TIMEOUT);
+                for (int s2 = max(0, s - NS); s2 < s; ++s2) mbar_wait_bounded(&full[s2 % NS], (s2 / NS) & 1);
+            }
+        }
+        return;
+    }
+
+    // scoring warps
+    const int nchunks = d >> 3;
+    float x[CHUNKS][8];
+    int cur = -1;
+    for (int s = 0;; ++s) {
+        const int slot = s % NS;
+        if (!mbar_wait_bounded(&full[slot], (s / NS) & 1)) {
+            if (lane == 0) atomicExch(status, LSA_ERR_TIMEOUT);
+            break;  // every scoring warp waits on the same phase and leaves here too
+        }
+        const StreamStage m = meta[slot];
+        if (m.row < 0) break;
+        if (m.row != cur) {
+            cur = m.row;
+#pragma unroll
+            for (int j = 0; j < CHUNKS; ++j) {
+                const int ch = lane + 32 * j;
+                if (ch < nchunks) load8<TQ>(q + cur * ldq + (size_t)ch * 8, x[j]);
+            }
+        }
+        const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(stage_buf + slot * kStreamStageBytes);
+        for (int cc = warp; cc < m.ncols; cc += kStreamWarps) {
+            const float p = butterfly_sum(lane_partial_regs<__nv_bfloat16, CHUNKS>(x, sc + (size_t)cc * d, lane, nchunks));
+            if (lane == 0) ws_keys[(int64_t)cur * N + m.col0 + cc] = pack_key(p, m.col0 + cc);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+}
+
+template <int KW>
+constexpr int finish_smem_bytes(int top_k) {
+    return (kFusedThreads / 32 + 1) * 32 * KW * 8 + kMemberPrefetch * 4 + top_k * 4;
+}
+
+// One CTA per row after select_stream_kernel: top K of the row's visible keys, the picked
+// member rows staged with 16-byte cp.async (cap % 4 == 0, 16-byte aligned members), the walk.
+template <int KW>
+__global__ void __launch_bounds__(kFusedThreads) select_finish_kernel(
+    const int64_t* __restrict__ ws_keys, int64_t N, RowPos rp, int64_t block, int64_t bpb, int top_p,
+    const int32_t* __restrict__ members, int cap, int window, int sink, int top_k, int32_t* __restrict__ lists,
+    int32_t* __restrict__ lengths) {
+    constexpr int K = 32 * KW, NW = kFusedThreads / 32;
+    extern __shared__ __align__(128) unsigned char fsm[];
+    int64_t* wlists = reinterpret_cast<int64_t*>(fsm);  // [NW][K]
+    int64_t* picks = wlists + NW * K;                    // [K]
+    int* mem = reinterpret_cast<int*>(picks + K);        // [kMemberPrefetch]
+    int* ostage = mem + kMemberPrefetch;                 // [top_k]
+    __shared__ int scan_smem[33];
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int count = (int)stream_visible(rp, r, N, block, bpb);
+    const int64_t Nr = rp.rows(r, N);
+    const int k = (int)min((int64_t)top_p, Nr);
+    GlobalKeysCg loader{ws_keys + (int64_t)r * N, count};
+    group_topk_desc<KW, NW>(loader, count, wlists, picks, warp, lane, BlockSync{});
+    const int32_t* mr = members + rp.off(r) * cap;
+    const int q4 = cap / 4;
+    for (int i = tid; i < k * q4; i += kFusedThreads) {
+        const int pk = i / q4, piece = i - pk * q4;
+        const int b = key_bucket(picks[pk]);
+        int* dst = mem + pk * cap + piece * 4;
+        if (b >= 0 && b < Nr) cp_async16(smem_u32(dst), mr + (int64_t)b * cap + piece * 4, 16);
+        else *reinterpret_cast<int4*>(dst) = make_int4(-1, -1, -1, -1);
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    const int width = top_k + window + sink;
+    expand_walk<kFusedThreads>(mem, k * cap, rp.walk_pos(r), window, sink, top_k, lists + (int64_t)r * width, width,
+                               lengths + r, scan_smem, tid, BlockSync{}, ostage);
+}
 
 template <typename K>
 static int set_smem(K kernel, int bytes) {
@@ -664,6 +902,12 @@ static int launch_scores(const void* q, int64_t R, int64_t ldq, const void* c, i
 using namespace lsa;
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+static int num_sms_select() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
 
 extern "C" {
 
@@ -784,7 +1028,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     int smem = sort_smem_bytes(most);
     if (smem < kFusedThreads * 8) smem = kFusedThreads * 8;
     if (smem < top_p * 8) smem = (int)(top_p * 8);
-    if (smem < k * 8 + staged * 4) smem = (int)(k * 8 + staged * 4);
+    if (smem < (k + 1) * 8 + staged * 4) smem = (int)((k + 1) * 8 + staged * 4);
     int ch = (int)((d / 8 + 31) / 32);
     cudaLaunchAttribute pdl;
     pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -802,8 +1046,72 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     int cs = (int)((most + 16 * cpw - 1) / (16 * cpw));
     if (cs < 1) cs = 1;
     bool use_cluster = !many_rows && cpw <= kMaxColsPerWarp && cs <= 16;
+    // rows wider than one cluster: the streaming scorer + per-row finish when their limits
+    // hold (bf16 centroids, top_p <= 128, staged members fit, 16-byte member rows, a status word)
+    if (!many_rows && !use_cluster && c_dtype == kBF16 && (q_dtype == kBF16 || q_dtype == kF32) &&
+        R <= kStreamMaxRows && top_p <= 128 && k * cap <= kMemberPrefetch && cap % 4 == 0 && aligned16(members) &&
+        top_k <= kFinishMaxTopK && n_counters >= R + 1 && d * 2 <= kStreamStageBytes && N < (1ll << 30)) {
+        int64_t items = R * ((most + kStreamItemCols - 1) / kStreamItemCols);
+        if (items < 1) items = 1;
+#define LSA_ST(TQ, CH)                                                                                              \
+    do {                                                                                                            \
+        auto kern = select_stream_kernel<TQ, CH>;                                                                   \
+        constexpr int ssm = kStreamStages * kStreamStageBytes;                                                      \
+        if (set_smem(kern, ssm)) return LSA_ERR_CUDA;                                                               \
+        int per_sm = 0;                                                                                             \
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kStreamThreads, ssm) != cudaSuccess ||     \
+            per_sm < 1)                                                                                             \
+            return LSA_ERR_CUDA;                                                                                    \
+        int64_t grid = (int64_t)per_sm * num_sms_select();                                                          \
+        if (grid > items) grid = items;                                                                             \
+        cudaLaunchConfig_t sc = {};                                                                                 \
+        sc.gridDim = dim3((unsigned)grid);                                                                          \
+        sc.blockDim = dim3(kStreamThreads);                                                                         \
+        sc.dynamicSmemBytes = ssm;                                                                                  \
+        sc.stream = stream;                                                                                         \
+        sc.attrs = &pdl;                                                                                            \
+        sc.numAttrs = 1;                                                                                            \
+        if (cudaLaunchKernelEx(&sc, kern, (const TQ*)queries, ldq, (const __nv_bfloat16*)centroids, N, (int)d,     \
+                               positions, block, bpb, (int)R, ws_keys, counters + R) != cudaSuccess)                \
+            return LSA_ERR_CUDA;                                                                                    \
+    } while (0)
+#define LSA_FIN(KW)                                                                                                 \
+    do {                                                                                                            \
+        auto fk = select_finish_kernel<KW>;                                                                         \
+        const int fsm = finish_smem_bytes<KW>((int)top_k);                                                          \
+        if (set_smem(fk, fsm)) return LSA_ERR_CUDA;                                                                 \
+        cudaLaunchConfig_t fc = {};                                                                                 \
+        fc.gridDim = dim3((unsigned)R);                                                                             \
+        fc.blockDim = dim3(kFusedThreads);                                                                          \
+        fc.dynamicSmemBytes = fsm;                                                                                  \
+        fc.stream = stream;                                                                                         \
+        fc.attrs = &pdl;                                                                                            \
+        fc.numAttrs = 1;                                                                                            \
+        if (cudaLaunchKernelEx(&fc, fk, (const int64_t*)ws_keys, N, positions, block, bpb, (int)top_p, members,     \
+                               (int)cap, (int)window, (int)sink, (int)top_k, lists, lengths) != cudaSuccess)        \
+            return LSA_ERR_CUDA;                                                                                    \
+    } while (0)
+        if (q_dtype == kBF16) {
+            if (ch <= 1) LSA_ST(__nv_bfloat16, 1);
+            else if (ch <= 2) LSA_ST(__nv_bfloat16, 2);
+            else if (ch <= 4) LSA_ST(__nv_bfloat16, 4);
+            else LSA_ST(__nv_bfloat16, 8);
+        } else {
+            if (ch <= 1) LSA_ST(float, 1);
+            else if (ch <= 2) LSA_ST(float, 2);
+            else if (ch <= 4) LSA_ST(float, 4);
+            else LSA_ST(float, 8);
+        }
+        if (top_p <= 32) LSA_FIN(1);
+        else if (top_p <= 64) LSA_FIN(2);
+        else LSA_FIN(4);
+#undef LSA_FIN
+#undef LSA_ST
+        LSA_LAUNCH_CHECK();
+        return LSA_OK;
+    }
     int csmem = sort_smem_bytes(most);
-    if (csmem < (k > 32 ? k : 32) * 8 + staged * 4) csmem = (int)((k > 32 ? k : 32) * 8 + staged * 4);
+    if (csmem < ((k > 32 ? k : 32) + 1) * 8 + staged * 4) csmem = (int)(((k > 32 ? k : 32) + 1) * 8 + staged * 4);
     if (csmem < k * 8) csmem = (int)(k * 8);
     if (csmem < cs * 16 * cpw * 8) csmem = cs * 16 * cpw * 8;  // every scored column's key slot
     cudaLaunchAttribute cattrs[2];

@@ -163,6 +163,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
+// TMA bulk copy (cp.async.bulk) of `bytes` contiguous bytes global -> shared, completion
+// counted in bytes on the mbarrier; both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // TMA gather of four rows (row0..row3) x one box of columns starting at col, into
 // consecutive box rows at dst (the tensor map's swizzle applies); completion counted in
 // bytes on the mbarrier. The map's box is one row high.

@@ -83,7 +83,7 @@ def batched_select(index_queries, positions, bb: BatchedBuckets, config, top_k=N
     pos = positions.to(torch.int32).contiguous()
     L = lib()
     sc = _lib.scratch(L.lsa_select_batched_scratch(R, bb.max_rows), dev)
-    ct = _lib.counters(R, dev)
+    ct = _lib.counters(R + 1, dev)  # tickets + the status word
     check(L.lsa_select_batched(ptr(q), _lib.DTYPE_CODE[q.dtype], R, d, ptr(c), _lib.DTYPE_CODE[c.dtype], d,
                                ptr(bb.table_off), ptr(bb.table_rows), bb.max_rows, ptr(pos),
                                config.cluster_block_size, config.block_bucket_count, ptr(bb.members),

@@ -372,7 +372,7 @@ def _select_fused(index_queries, positions, buckets, config, top_k, score_dtype)
     L = lib()
     nbytes = L.lsa_select_fused_scratch(R, N)
     sc = _lib.scratch(nbytes, dev)
-    ct = _lib.counters(R, dev)
+    ct = _lib.counters(R + 1, dev)  # tickets + the status word
     check(L.lsa_select_fused(ptr(q), _lib.DTYPE_CODE[q.dtype], R, d, ptr(c.contiguous()), _lib.DTYPE_CODE[c.dtype],
                              N, d, ptr(pos), config.cluster_block_size, config.block_bucket_count,
                              ptr(buckets.members), buckets.members.shape[1], config.top_p, config.window_size,

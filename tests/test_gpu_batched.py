@@ -84,3 +84,40 @@ def test_batched_select_rejects_mismatched_tables(lsa):
     bb = batched.concat_buckets(per_seq[:1])
     with pytest.raises(ValueError):
         batched.batched_select(iq, pos, bb, cfg)
+
+
+STREAM_CASES = [
+    # (Hkv, D, bucket, cap, top_p, top_k): index width d = Hkv * D sets the columns per 32 KB stage
+    (8, 128, 64, 128, 64, 4096),  # the 128k configuration: d = 1024, 16 columns per stage
+    (2, 64, 32, 64, 128, 4096),  # d = 128: one 128-column item per stage, top-128 lists
+    (4, 64, 64, 128, 32, 2048),  # d = 256, top-32
+]
+
+
+@pytest.mark.parametrize("Hkv,D,bucket,cap,top_p,top_k", STREAM_CASES)
+def test_batched_select_wide_rows_stream_kernel(lsa, Hkv, D, bucket, cap, top_p, top_k):
+    """Rows wider than one cluster (> 1024 visible buckets) take the persistent streaming
+    kernel: every row equals the reference arm of flat_select on its own sequence, byte for
+    byte, including a sequence shorter than a block and lengths off the block grid; the
+    fused flat_select of one wide row (the same kernel, R = 1) agrees too; a replay gives
+    the same lists (the tickets return to zero)."""
+    from lsa_b200 import batched
+
+    cfg = lsa.PortConfig(cluster_block_size=512, pool_size=4, bucket_size=bucket, bucket_cap=cap, top_p=top_p,
+                         top_k=top_k, window_size=64, sink_size=4)
+    lengths = [70001, 131072, 300, 99999, 66560]
+    q, k, v, iq, pos, per_seq = _case(lsa, lengths, Hkv * 2, Hkv, D, cfg, 21)
+    bb = batched.concat_buckets(per_seq)
+    assert bb.max_rows > 1024
+    gl, gn = batched.batched_select(iq, pos, bb, cfg)
+    gl2, gn2 = batched.batched_select(iq, pos, bb, cfg)
+    assert torch.equal(gl, gl2) and torch.equal(gn, gn2)
+    for impl in ("reference", "fused"):
+        os.environ["LSA_SELECT_IMPL"] = impl
+        try:
+            for b in range(len(lengths)):
+                wl, wn = lsa.flat_select(iq[b:b + 1], pos[b:b + 1], per_seq[b], cfg)
+                assert torch.equal(gl[b:b + 1], wl) and torch.equal(gn[b:b + 1], wn), (impl, b)
+        finally:
+            os.environ.pop("LSA_SELECT_IMPL", None)
+    assert int(gn[2]) == 64 + 4  # shorter than a block: window + sinks only
