@@ -480,7 +480,7 @@ def run_prefill(args, dev):
                      "peak": tflops, "unit": "TFLOP/s", "frac": round(achieved / tflops, 4), "peak_kind": peak_kind,
                      "traffic": _traffic_from_profile("sparse_prefill_32k.md")},
         "clocks": clocks.summary(),
-        "gpu_launches_per_step": 1 + 2 + 1,  # tile queries, fused select (+ its fallback never), read
+        "gpu_launches_per_step": 3,  # tile queries, the one-CTA-per-tile fused select, the tcgen05 read
     }
 
 
@@ -618,7 +618,9 @@ def run_batched(args, rank, world, dev):
                    "l2": "no flush: one step reads > 1 GB of K/V"},
         "us_per_step": round(ms * 1e3, 2), "us_select": round(us_select, 2), "us_read": round(us_read, 2),
         "sequences": all_seqs, "bytes_per_step": int(all_bytes),
-        "gpu_launches": args.steps * 2, "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
+        # per step: the read, and the selection - one launch, or two (streaming scorer + per-row
+        # finish) when the widest row has more than 1024 buckets (more than one cluster)
+        "gpu_launches": args.steps * (1 + (2 if bb.max_rows > 1024 else 1)), "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
         "clocks": clocks.summary(),
     }
 

@@ -115,6 +115,7 @@ struct ReadArgs {
     float* part_ml;  // [R*Hkv, splits, G, 2]
     int32_t* tickets;
     int32_t* status;
+    int32_t* queue;  // persistent read: [0] next work item, [1] CTAs done (zero at rest)
     int64_t Tq, Tk;
     int Hq, Hkv, G, width, splits, span, combine;
     float scale_log2;  // scale * log2(e)
@@ -138,6 +139,118 @@ __device__ __forceinline__ void write_out(const ReadArgs& a, int64_t rq, int e, 
     }
 }
 
+// The last CTA of unit rh (row * Hkv + h) merges the splits' partials (part_o / part_ml in
+// global memory) and writes the output: the split weights are staged in shared memory
+// (wts: splits * G + 2 G floats), then every output sums its splits with independent loads.
+struct CtaSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+template <typename T, int D, typename Sync = CtaSync>
+__device__ void merge_splits(const ReadArgs& a, int rh, int64_t row, int h, float* wts, int tid, Sync sync = Sync{}) {
+    const int G = a.G;
+    float* tot = wts + a.splits * G;  // [G] totals, then [G] maxima
+    float* wmax = tot + G;
+    for (int i = tid; i < a.splits * G; i += kReadThreads) wts[i] = __ldcg(a.part_ml + ((int64_t)rh * a.splits * G + i) * 2);
+    sync();
+    if (tid < G) {
+        float M = kNegBig;
+        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, wts[sp * G + tid]);
+        float L = 0.0f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+            float f = exp2f(wts[sp * G + tid] - M);
+            L += __ldcg(a.part_ml + (((int64_t)rh * a.splits + sp) * G + tid) * 2 + 1) * f;
+            wts[sp * G + tid] = f;
+        }
+        tot[tid] = L;
+        wmax[tid] = M;
+    }
+    sync();
+    for (int o = tid; o < G * D; o += kReadThreads) {
+        int g = o / D, e = o % D;
+        float O = 0.0f;
+#pragma unroll 8
+        for (int sp = 0; sp < a.splits; ++sp)
+            O += wts[sp * G + g] * __ldcg(a.part_o + (((int64_t)rh * a.splits + sp) * G + g) * D + e);
+        write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, wmax[g], tot[g]);
+    }
+}
+
+// One stage of the tensor-core path for one warp: the warp's SPW = 8 J staged slots (K rows
+// at kaddr, V rows at vaddr, row stride D + 8 elements, listed flags fl). S = q K^T as
+// mma.m16n8k16 with the query heads as M (rows >= G are zero); the scores stay in registers
+// and become the P operand of O += P V (FA2 fragment reuse); (mrow, lrow) is the running
+// max / sum of row lane / 4 in the exp2 domain.
+template <typename T, int D, int J>
+__device__ __forceinline__ void mma_stage(uint32_t kaddr, uint32_t vaddr, const unsigned char* fl,
+                                          const uint32_t (&qa)[D / 16][2], float (&o)[D / 8][4], float& mrow,
+                                          float& lrow, float scale_log2, int lane) {
+    constexpr int ROWS = D + 8, DC = D / 16, NT = D / 8, SPW = 8 * J;
+    const int tq = lane & 3;
+    float sc[J][4];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+        for (int q4 = 0; q4 < DC / 2; ++q4) {  // 4 dim blocks of 8 per ldmatrix.x4
+            uint32_t b0, b1, b2, b3;
+            uint32_t addr = kaddr + ((8 * j + (lane & 7)) * ROWS + (4 * q4 + (lane >> 3)) * 8) * 2;
+            ldsm_x4(addr, b0, b1, b2, b3);
+            mma16816<T>(sc[j], qa[2 * q4][0], 0u, qa[2 * q4][1], 0u, b0, b1);
+            mma16816<T>(sc[j], qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
+        }
+    }
+    // scores of row gq for keys 8j + 2tq + {0, 1}; unlisted slots never count
+    float sv[2 * J];
+    float mx = kNegBig;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            bool valid = fl[8 * j + 2 * tq + e] != 0;
+            float v = valid ? sc[j][e] * scale_log2 : -INFINITY;
+            sv[2 * j + e] = v;
+            mx = fmaxf(mx, v);
+        }
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+    float mnew = fmaxf(mrow, mx);
+    float alpha = exp2f(mrow - mnew);
+    mrow = mnew;
+    float p[2 * J];
+    float psum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2 * J; ++i) {
+        p[i] = exp2f(sv[i] - mnew);
+        psum += p[i];
+    }
+    lrow = lrow * alpha + psum;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        o[nt][0] *= alpha;
+        o[nt][1] *= alpha;
+    }
+    // the P operand covers k16 = 16 keys; with 8 slots per warp its upper half is zero
+    uint32_t pa0 = pack2<T>(p[0], p[1]), pa2 = J == 2 ? pack2<T>(p[2 % (2 * J)], p[3 % (2 * J)]) : 0u;
+    // V rows of unlisted slots hold stale shared memory: zero their fragment halves
+    // (b0/b2 carry keys 2tq, 2tq + 1; b1/b3 keys 8 + 2tq, 9 + 2tq) so 0 * garbage
+    // cannot turn into NaN inside the MMA
+    const uint32_t vm0 = (fl[2 * tq] ? 0x0000FFFFu : 0u) | (fl[2 * tq + 1] ? 0xFFFF0000u : 0u);
+    const uint32_t vm1 = J == 2 ? ((fl[(8 + 2 * tq) % SPW] ? 0x0000FFFFu : 0u) |
+                                   (fl[(9 + 2 * tq) % SPW] ? 0xFFFF0000u : 0u))
+                                : 0u;
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        // with 8 slots the upper key half re-reads this warp's rows (masked to zero)
+        int key = (lane & 7) + (J == 2 ? 8 * ((lane >> 3) & 1) : 0);
+        int dblk = 2 * np + (lane >> 4);
+        ldsm_x4_t(vaddr + (key * ROWS + dblk * 8) * 2, b0, b1, b2, b3);
+        mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
+        mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
+    }
+}
+
 template <typename T, int D, int GMAX>
 __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     constexpr int STAGE = StageIds<T>::value;
@@ -152,6 +265,9 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     constexpr int ROWB = D * sizeof(T);       // bytes copied per row
     constexpr int STAGE_BYTES = STAGE * ROWS * (int)sizeof(T);
     constexpr int IDW = STAGE / NW;     // id slots a warp issues per stage
+    constexpr int SPW = IDW;            // slots a warp computes per stage (tensor-core path)
+    constexpr int J = SPW / 8;          // n8 key tiles per warp
+    static_assert(SPW == 8 || SPW == 16, "a warp computes one or two n8 key tiles");
     static_assert(2 * IDW <= 32, "a warp issues the K and V rows of its slots in one pass");
     constexpr int NST = kReadStages;
     extern __shared__ __align__(128) unsigned char smem[];
@@ -262,76 +378,13 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
                 failed = true;
                 break;
             }
-            const int kb = warp * 16;  // first slot of this warp
+            const int kb = warp * SPW;  // first slot of this warp
             const unsigned char* fl = sflag + buf * STAGE + kb;
-            bool any = __any_sync(0xFFFFFFFFu, lane < 16 && fl[lane & 15]);
-            if (any) {
-                const uint32_t kaddr = smem_u32(sK + ((size_t)buf * STAGE + kb) * ROWS);
-                const uint32_t vaddr = smem_u32(sV + ((size_t)buf * STAGE + kb) * ROWS);
-                float sc[2][4];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    // two accumulator chains per key tile (even / odd k16 blocks), summed after:
-                    // half the dependent MMA latency of one chain
-                    float s2[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
-#pragma unroll
-                    for (int q4 = 0; q4 < DC / 2; ++q4) {  // 4 dim blocks of 8 per ldmatrix.x4
-                        uint32_t b0, b1, b2, b3;
-                        uint32_t addr = kaddr + ((8 * j + (lane & 7)) * ROWS + (4 * q4 + (lane >> 3)) * 8) * 2;
-                        ldsm_x4(addr, b0, b1, b2, b3);
-                        mma16816<T>(sc[j], qa[2 * q4][0], 0u, qa[2 * q4][1], 0u, b0, b1);
-                        mma16816<T>(s2, qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) sc[j][e] += s2[e];
-                }
-                // scores of row gq for keys 8j + 2tq + {0, 1}; unlisted slots never count
-                float sv[4];
-                float mx = kNegBig;
-#pragma unroll
-                for (int j = 0; j < 2; ++j)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        bool valid = fl[8 * j + 2 * tq + e] != 0;
-                        float v = valid ? sc[j][e] * a.scale_log2 : -INFINITY;
-                        sv[2 * j + e] = v;
-                        mx = fmaxf(mx, v);
-                    }
-                mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
-                float mnew = fmaxf(mrow, mx);
-                float alpha = exp2f(mrow - mnew);
-                mrow = mnew;
-                float p[4];
-                float psum = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    p[i] = exp2f(sv[i] - mnew);
-                    psum += p[i];
-                }
-                lrow = lrow * alpha + psum;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    o[nt][0] *= alpha;
-                    o[nt][1] *= alpha;
-                }
-                uint32_t pa0 = pack2<T>(p[0], p[1]), pa2 = pack2<T>(p[2], p[3]);
-                // V rows of unlisted slots hold stale shared memory: zero their fragment halves
-                // (b0/b2 carry keys 2tq, 2tq + 1; b1/b3 keys 8 + 2tq, 9 + 2tq) so 0 * garbage
-                // cannot turn into NaN inside the MMA
-                const uint32_t vm0 = (fl[2 * tq] ? 0x0000FFFFu : 0u) | (fl[2 * tq + 1] ? 0xFFFF0000u : 0u);
-                const uint32_t vm1 = (fl[8 + 2 * tq] ? 0x0000FFFFu : 0u) | (fl[9 + 2 * tq] ? 0xFFFF0000u : 0u);
-#pragma unroll
-                for (int np = 0; np < NT / 2; ++np) {
-                    uint32_t b0, b1, b2, b3;
-                    int key = (lane & 7) + 8 * ((lane >> 3) & 1);
-                    int dblk = 2 * np + (lane >> 4);
-                    ldsm_x4_t(vaddr + (key * ROWS + dblk * 8) * 2, b0, b1, b2, b3);
-                    mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
-                    mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
-                }
-            }
+            bool any = __any_sync(0xFFFFFFFFu, lane < SPW && fl[lane % SPW]);
+            if (any)
+                mma_stage<T, D, J>(smem_u32(sK + ((size_t)buf * STAGE + kb) * ROWS),
+                                   smem_u32(sV + ((size_t)buf * STAGE + kb) * ROWS), fl, qa, o, mrow, lrow,
+                                   a.scale_log2, lane);
             __syncthreads();  // every warp is done with this buffer
             if (st + NST < n_stages) {
                 issue(st + NST, id_next);
@@ -543,38 +596,282 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // stage the split weights, then every output sums its splits with independent loads
-    float* wts = red;  // [splits][G] weights, then [G] totals and [G] maxima
-    float* tot = red + a.splits * G;
-    float* wmax = tot + G;
-    for (int i = tid; i < a.splits * G; i += kReadThreads) wts[i] = __ldcg(a.part_ml + ((int64_t)rh * a.splits * G + i) * 2);
-    __syncthreads();
-    if (tid < G) {
-        float M = kNegBig;
-        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, wts[sp * G + tid]);
-        float L = 0.0f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-            float f = exp2f(wts[sp * G + tid] - M);
-            L += __ldcg(a.part_ml + (((int64_t)rh * a.splits + sp) * G + tid) * 2 + 1) * f;
-            wts[sp * G + tid] = f;
+    merge_splits<T, D>(a, rh, row, h, red, tid);
+}
+
+// ------------------------------------------------------------------ persistent read
+
+// Bandwidth-bound batches (many (row, KV head) units, 16-bit inputs): a persistent grid of
+// one CTA per SM takes work items = (row, split, KV head) from a global queue (atomic
+// counter: SMs that run slower take fewer items). Four producer warps feed a ring of three
+// 128-id stages with 16-byte cp.async row pieces (full / empty mbarriers) while eight
+// consumer warps run the tensor-core stage, so the copy issue never waits behind the math
+// (measured: 256-byte TMA bulk copies per row issue too slowly for this - the SM takes one
+// every ~10-15 cycles and a warp's copy instruction issues its lanes one after another).
+// The ring spans items: the next item's rows are in flight while the current one finishes
+// (no per-CTA prologue, no partly filled last wave). At an item's last stage the consumer
+// warps merge their partials in the consumed stage (before releasing it), write the
+// item's split partial, and the unit's last split (atomic ticket) writes the output with
+// merge_splits. Queue counters: [0] next item, [1] CTAs done; the last CTA resets both.
+constexpr int kPersistStage = 128;    // ids per stage
+constexpr int kPersistProducers = 4;  // producer warps
+constexpr int kPersistThreads = kReadThreads + 32 * kPersistProducers;
+
+template <typename T, int D, int GMAX>
+constexpr int persist_smem_bytes() {
+    return 2 * kReadStages * kPersistStage * (D + 8) * (int)sizeof(T);
+}
+
+struct ConsumerSync {  // the consumer warps' named barrier (the producer warps never join it)
+    __device__ __forceinline__ void operator()() const {
+        asm volatile("bar.sync 1, %0;" ::"n"(kReadThreads) : "memory");
+    }
+};
+
+__device__ __forceinline__ void producer_sync() {
+    asm volatile("bar.sync 2, %0;" ::"n"(32 * kPersistProducers) : "memory");
+}
+
+// Named-barrier vote: true on every participating thread when any of them passes true, so
+// a wait that expired on one thread sends the whole group out together.
+template <int BAR, int COUNT>
+__device__ __forceinline__ bool group_any(bool x) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)x), "n"(BAR), "n"(COUNT)
+        : "memory");
+    return r != 0;
+}
+
+// cp.async completion tracking without a reserved arrival: the barrier's pending count
+// rises now and falls when this thread's earlier cp.async copies land
+__device__ __forceinline__ void cp_async_track(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+struct PersistStage {
+    int rh, split, first, last;  // rh < 0: no more work
+};
+
+template <typename T, int D, int GMAX>
+__global__ void __launch_bounds__(kPersistThreads, 1) sparse_read_persist_kernel(ReadArgs a, int n_items) {
+    constexpr int STAGE = kPersistStage;
+    constexpr int NW = kReadThreads / 32;  // consumer warps
+    constexpr int SPW = STAGE / NW;        // slots a consumer warp computes per stage (16)
+    constexpr int J = SPW / 8;
+    constexpr int NST = kReadStages;
+    constexpr int ROWS = D + 8;
+    constexpr int ROWB = D * sizeof(T);
+    constexpr int STAGE_BYTES = STAGE * ROWS * (int)sizeof(T);  // the K (or V) rows of one stage
+    constexpr int DC = D / 16, NT = D / 8;
+    constexpr int NP = 32 * kPersistProducers;
+    static_assert(sizeof(T) == 2, "tensor-core path only");
+    static_assert(STAGE == NP, "a producer thread owns one slot of every stage");
+    static_assert(NW * GMAX * D * 4 + NW * GMAX * 2 * 4 <= 2 * STAGE_BYTES, "the warp partials fit one stage");
+    // stage buf = its K rows then its V rows (contiguous, so the warp partials of an item's
+    // last stage can use the whole consumed stage)
+    extern __shared__ __align__(128) unsigned char smem[];
+    auto stage_k = [&](int buf) { return reinterpret_cast<T*>(smem + (size_t)buf * 2 * STAGE_BYTES); };
+    auto stage_v = [&](int buf) { return reinterpret_cast<T*>(smem + ((size_t)buf * 2 + 1) * STAGE_BYTES); };
+    __shared__ __align__(8) uint64_t full[NST], empty[NST];
+    __shared__ unsigned char sflag[NST * STAGE];
+    __shared__ PersistStage smeta[NST];
+    __shared__ int pdesc[2][4];  // the producers' current item: rh, split, s0, s1 (rh < 0: stop)
+    __shared__ int is_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = a.G;
+    if (tid == 0) {
+#pragma unroll
+        for (int i = 0; i < NST; ++i) {
+            mbar_init(&full[i], NP);   // one release arrival per producer thread (+ its tracked copies)
+            mbar_init(&empty[i], NW);  // one arrival per consumer warp
         }
-        tot[tid] = L;
-        wmax[tid] = M;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    for (int o = tid; o < G * D; o += kReadThreads) {
-        int g = o / D, e = o % D;
-        float O = 0.0f;
+    pdl_wait();
+    pdl_trigger();
+
+    if (warp >= NW) {  // producer warps: producer thread pt copies slot pt of every stage
+        const int pt = tid - kReadThreads;
+        bool ok = true;
+        int g = 0;
+        for (int seq = 0;; ++seq) {
+            int* d = pdesc[seq & 1];
+            if (pt == 0) {
+                const int it = atomicAdd(a.queue, 1);
+                if (it >= n_items) {
+                    d[0] = -1;
+                    // every CTA takes items until the queue runs dry, then counts itself done;
+                    // the last one resets the queue for the next launch
+                    if (atomicAdd(a.queue + 1, 1) == (int)gridDim.x - 1) {
+                        a.queue[0] = 0;
+                        a.queue[1] = 0;
+                    }
+                } else {
+                    // item order (row, split, KV head), heads fastest: the Hkv items that read
+                    // the same positions of a row are taken side by side
+                    const int h = it % a.Hkv, rs = it / a.Hkv;
+                    const int split = rs % a.splits;
+                    const int rh = (rs / a.splits) * a.Hkv + h;
+                    int len = a.lengths[rh / a.Hkv];
+                    len = len < 0 ? 0 : (len > a.width ? a.width : len);
+                    const int s0 = split * a.span;
+                    d[0] = rh;
+                    d[1] = split;
+                    d[2] = s0;
+                    d[3] = max(s0, min(s0 + a.span, len));
+                }
+            }
+            producer_sync();
+            const int rh = d[0], split = d[1], s0 = d[2], s1 = d[3];
+            // an item with no id keeps one empty stage, so its split still posts a partial
+            const int n_st = rh < 0 ? 1 : max(1, (s1 - s0 + STAGE - 1) / STAGE);
+            const int64_t row = rh < 0 ? 0 : rh / a.Hkv;
+            const int h = rh < 0 ? 0 : rh % a.Hkv;
+            const int64_t kv0 = ((row / a.Tq) * a.Tk * a.Hkv + h) * D;  // (b, position 0, h)
+            for (int st = 0; st < n_st; ++st, ++g) {
+                const int buf = g % NST;
+                const bool waited = mbar_wait_bounded(&empty[buf], ((g / NST) & 1) ^ 1);
+                if (group_any<2, 32 * kPersistProducers>(!waited)) {
+                    ok = false;
+                    break;
+                }
+                if (pt == 0) smeta[buf] = PersistStage{rh, split, st == 0, st == n_st - 1};
+                int id = -1;
+                if (rh >= 0) {
+                    const int at = s0 + st * STAGE + pt;  // coalesced id loads
+                    id = at < s1 ? a.ids[row * a.width + at] - a.id_base : -1;
+                    if (id >= a.Tk) id = -1;
+                }
+                sflag[buf * STAGE + pt] = id >= 0 ? 1 : 0;
+                // 16-byte pieces of the warp's 32 slots: lanes 0-15 a slot's K row, 16-31 its V row
+                const int piece = lane & 15;
+                const bool v_half = lane >= 16;
+                const int slot0 = pt - lane;
+                T* dst0 = (v_half ? stage_v(buf) : stage_k(buf)) + (size_t)slot0 * ROWS + piece * (16 / (int)sizeof(T));
+                const T* src0 = reinterpret_cast<const T*>(v_half ? a.v : a.k) + kv0 + piece * (16 / (int)sizeof(T));
 #pragma unroll 8
-        for (int sp = 0; sp < a.splits; ++sp)
-            O += wts[sp * G + g] * __ldcg(a.part_o + (((int64_t)rh * a.splits + sp) * G + g) * D + e);
-        write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, wmax[g], tot[g]);
+                for (int j = 0; j < 32; ++j) {
+                    const int idj = __shfl_sync(0xFFFFFFFFu, id, j);
+                    if (idj >= 0 && piece * 16 < ROWB)
+                        cp_async16(smem_u32(dst0 + (size_t)j * ROWS), src0 + (int64_t)idj * a.Hkv * D, 16);
+                }
+                cp_async_track(&full[buf]);  // the phase also waits for these copies
+                mbar_arrive(&full[buf]);      // release: the slot flags and stage record above
+            }
+            if (!ok || rh < 0) break;
+        }
+        if (!ok && lane == 0) {  // the consumers stopped: wait (bounded) for the copies in flight
+            atomicExch(a.status, LSA_ERR_TIMEOUT);
+            for (int s2 = max(0, g - NST); s2 < g; ++s2) mbar_wait_bounded(&full[s2 % NST], (s2 / NST) & 1);
+        }
+        return;
+    }
+
+    // consumer warps
+    const int gq = lane >> 2, tq = lane & 3;
+    uint32_t qa[DC][2];
+    float o[NT][4];
+    float mrow = kNegBig, lrow = 0.0f;
+    for (int g = 0;; ++g) {
+        const int buf = g % NST;
+        const bool waited = mbar_wait_bounded(&full[buf], (g / NST) & 1);
+        if (group_any<1, kReadThreads>(!waited)) {  // the consumers leave together
+            if (tid == 0) atomicExch(a.status, LSA_ERR_TIMEOUT);
+            return;
+        }
+        const PersistStage m = smeta[buf];
+        if (m.rh < 0) return;  // no more work (the stop stage is never released)
+        const int rh = m.rh;
+        const int64_t row = rh / a.Hkv;
+        const int h = rh % a.Hkv;
+        if (m.first) {  // a new item: its query rows, fresh state
+#pragma unroll
+            for (int dc = 0; dc < DC; ++dc) {
+                const T* qp = reinterpret_cast<const T*>(a.q) + ((row * a.Hq) + h * G + gq) * D + dc * 16 + 2 * tq;
+                qa[dc][0] = gq < G ? *reinterpret_cast<const uint32_t*>(qp) : 0u;
+                qa[dc][1] = gq < G ? *reinterpret_cast<const uint32_t*>(qp + 8) : 0u;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+            mrow = kNegBig;
+            lrow = 0.0f;
+        }
+        const unsigned char* fl = sflag + buf * STAGE + warp * SPW;
+        if (__any_sync(0xFFFFFFFFu, lane < SPW && fl[lane % SPW]))
+            mma_stage<T, D, J>(smem_u32(stage_k(buf) + (size_t)warp * SPW * ROWS),
+                               smem_u32(stage_v(buf) + (size_t)warp * SPW * ROWS), fl, qa, o, mrow, lrow,
+                               a.scale_log2, lane);
+        if (m.last) {
+            // the item's last stage: the warps' partials meet in this consumed stage
+            ConsumerSync{}();
+            float* red = reinterpret_cast<float*>(stage_k(buf));  // [NW][GMAX][D]
+            float* redml = red + NW * GMAX * D;                    // [NW][GMAX][2]
+            float l4 = lrow;
+            l4 += __shfl_xor_sync(0xFFFFFFFFu, l4, 1);
+            l4 += __shfl_xor_sync(0xFFFFFFFFu, l4, 2);
+            if (gq < G) {
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    red[(warp * GMAX + gq) * D + nt * 8 + 2 * tq] = o[nt][0];
+                    red[(warp * GMAX + gq) * D + nt * 8 + 2 * tq + 1] = o[nt][1];
+                }
+                if (tq == 0) {
+                    redml[(warp * GMAX + gq) * 2] = mrow;
+                    redml[(warp * GMAX + gq) * 2 + 1] = l4;
+                }
+            }
+            ConsumerSync{}();
+            for (int oi = tid; oi < G * D; oi += kReadThreads) {
+                const int gg = oi / D, e = oi % D;
+                float M = kNegBig;
+#pragma unroll
+                for (int r = 0; r < NW; ++r) M = fmaxf(M, redml[(r * GMAX + gg) * 2]);
+                float L = 0.0f, O = 0.0f;
+#pragma unroll
+                for (int r = 0; r < NW; ++r) {
+                    const float f = exp2f(redml[(r * GMAX + gg) * 2] - M);
+                    L += redml[(r * GMAX + gg) * 2 + 1] * f;
+                    O += red[(r * GMAX + gg) * D + e] * f;
+                }
+                const int64_t pidx = ((int64_t)rh * a.splits + m.split) * G + gg;
+                a.part_o[pidx * D + e] = O;
+                if (e == 0) {
+                    a.part_ml[pidx * 2] = M;
+                    a.part_ml[pidx * 2 + 1] = L;
+                }
+            }
+            __threadfence();
+            ConsumerSync{}();
+            if (tid == 0) {
+                const int t = atomicAdd(a.tickets + rh, 1);
+                is_last = t == a.splits - 1;
+                if (is_last) a.tickets[rh] = 0;
+            }
+            ConsumerSync{}();
+            if (is_last) {
+                __threadfence();
+                merge_splits<T, D>(a, rh, row, h, red, tid, ConsumerSync{});
+            }
+            ConsumerSync{}();  // every consumer is done with the stage
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[buf]);
     }
 }
 
 struct ReadPlan {
     int splits, span, combine;
     int64_t part_o_bytes, part_ml_bytes, scratch_bytes, counters;
+    bool persist = false;  // 16-bit inputs take sparse_read_persist_kernel over `grid` CTAs
+    int64_t grid = 0;
 };
 
 static int num_sms() {
@@ -610,6 +907,8 @@ static const int* cluster_capacity() {
         auto kern = sparse_read_kernel<__nv_bfloat16, 128, 8>;
         constexpr int smem = read_smem_bytes<__nv_bfloat16, 128, 8>();
         bool ok = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+                  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       cudaSharedmemCarveoutMaxShared) == cudaSuccess &&
                   cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
         for (int c = 0; c <= kMaxClusterSplits; ++c) {
             table[dev][c] = 0;
@@ -637,10 +936,33 @@ static const int* cluster_capacity() {
 // splits: CTAs per (row, KV head). Auto (splits_req <= 0): about four CTAs per SM over the
 // whole launch, at least 128 ids per split, at most one cluster. A count above the cluster
 // limit merges through the ticket path.
-static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t width, int64_t splits_req, int sms) {
+static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t width, int64_t splits_req, int sms,
+                          bool allow_persist = true) {
     ReadPlan p;
-    const int* cap = cluster_capacity();
     int64_t units = R * Hkv;
+    if (splits_req <= 0 && allow_persist && units >= 2 * (int64_t)sms && width > 0 && (D == 64 || D == 128)) {
+        // bandwidth-bound batch: persistent grid (one CTA per SM), about four items per CTA
+        // (measured best: more items balance better but each adds a split merge), at least
+        // 512 ids per item; splits merge by ticket
+        const int64_t slots = (int64_t)sms;
+        int64_t s = (4 * slots + units - 1) / units;
+        int64_t by_len = width / 512;
+        if (s > by_len) s = by_len;
+        if (s < 1) s = 1;
+        const int64_t items = units * s;
+        const int64_t grid = items < slots ? items : slots;
+        p.splits = (int)s;
+        p.span = (int)((width + s - 1) / s);
+        p.combine = kTicket;
+        p.persist = true;
+        p.grid = grid;
+        p.part_o_bytes = round256(units * s * G * D * 4);
+        p.part_ml_bytes = round256(units * s * G * 2 * 4);
+        p.scratch_bytes = p.part_o_bytes + p.part_ml_bytes;
+        p.counters = units + 3;  // tickets, the status word, the work queue and its done count
+        return p;
+    }
+    const int* cap = cluster_capacity();
     int64_t s = splits_req;
     if (s <= 0) {
         int64_t target = 4 * (int64_t)sms;
@@ -670,7 +992,10 @@ template <typename T, int D, int GMAX>
 static int launch_read(const ReadArgs& a, int64_t ctas, cudaStream_t st) {
     constexpr int smem = read_smem_bytes<T, D, GMAX>();
     auto kern = sparse_read_kernel<T, D, GMAX>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    // the largest shared-memory carveout, so two 16-bit CTAs (three stages each) share an SM
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+            cudaSuccess)
         return LSA_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas);
@@ -698,6 +1023,37 @@ static int launch_read(const ReadArgs& a, int64_t ctas, cudaStream_t st) {
     return LSA_OK;
 }
 
+template <typename T, int D, int GMAX>
+static int launch_persist(const ReadArgs& a, int64_t grid, int n_items, cudaStream_t st) {
+    constexpr int smem = persist_smem_bytes<T, D, GMAX>();
+    auto kern = sparse_read_persist_kernel<T, D, GMAX>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+            cudaSuccess)
+        return LSA_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kPersistThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, a, n_items) != cudaSuccess) return LSA_ERR_CUDA;
+    return LSA_OK;
+}
+
+template <typename T, int D>
+static int dispatch_persist(const ReadArgs& a, int64_t grid, int n_items, cudaStream_t st) {
+    if (a.G <= 1) return launch_persist<T, D, 1>(a, grid, n_items, st);
+    if (a.G <= 2) return launch_persist<T, D, 2>(a, grid, n_items, st);
+    if (a.G <= 4) return launch_persist<T, D, 4>(a, grid, n_items, st);
+    if (a.G <= 8) return launch_persist<T, D, 8>(a, grid, n_items, st);
+    return LSA_ERR_ARG;
+}
+
 template <typename T, int D>
 static int dispatch_g(const ReadArgs& a, int64_t ctas, cudaStream_t st) {
     if (a.G <= 1) return launch_read<T, D, 1>(a, ctas, st);
@@ -718,7 +1074,7 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
                        const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D,
                        int64_t width, float scale, void* out, void* scratch, int64_t scratch_bytes, int32_t* counters,
                        int64_t n_counters, int64_t splits, cudaStream_t stream, int64_t id_base = 0,
-                       float* out32 = nullptr, float* lse = nullptr) {
+                       float* out32 = nullptr, float* lse = nullptr, bool allow_persist = true) {
     if (B < 0 || Tq < 0 || Tk < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || width < 0) return LSA_ERR_ARG;
     if (D != 64 && D != 128) return LSA_ERR_ARG;
     if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out | (uintptr_t)scratch | (uintptr_t)out32) & 15)
@@ -728,7 +1084,7 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     if (R == 0) return LSA_OK;
     int64_t G = Hq / Hkv;
     if (G > 8) return LSA_ERR_ARG;
-    ReadPlan p = plan_read(R, Hkv, G, D, width, splits, num_sms());
+    ReadPlan p = plan_read(R, Hkv, G, D, width, splits, num_sms(), allow_persist);
     if (scratch_bytes < p.scratch_bytes || n_counters < p.counters || !counters) return LSA_ERR_ARG;
     char* w = (char*)scratch;
     ReadArgs a;
@@ -737,6 +1093,7 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     a.part_ml = (float*)(w + p.part_o_bytes);
     a.tickets = counters;
     a.status = counters + R * Hkv;
+    a.queue = counters + R * Hkv + 1;
     a.Tq = Tq; a.Tk = Tk;
     a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.G = (int)G; a.width = (int)width;
     a.splits = p.splits; a.span = p.span; a.combine = p.combine;
@@ -745,6 +1102,14 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     a.out32 = out32;
     a.lse = lse;
     int64_t ctas = R * Hkv * p.splits;
+    if (p.persist && (dtype == kBF16 || dtype == kF16)) {
+        const int n_items = (int)ctas;
+        if (dtype == kBF16)
+            return D == 64 ? dispatch_persist<__nv_bfloat16, 64>(a, p.grid, n_items, stream)
+                           : dispatch_persist<__nv_bfloat16, 128>(a, p.grid, n_items, stream);
+        return D == 64 ? dispatch_persist<__half, 64>(a, p.grid, n_items, stream)
+                       : dispatch_persist<__half, 128>(a, p.grid, n_items, stream);
+    }
     if (dtype == kBF16) return dispatch_d<__nv_bfloat16>(a, (int)D, ctas, stream);
     if (dtype == kF16) return dispatch_d<__half>(a, (int)D, ctas, stream);
     if (dtype == kF32) return dispatch_d<float>(a, (int)D, ctas, stream);
@@ -903,7 +1268,9 @@ int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dty
                             const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
                             int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream) {
     if (Hkv <= 0 || Hq % Hkv || width < 0 || D <= 0) return LSA_ERR_ARG;
-    lsa::ReadPlan p = lsa::plan_read(B * Tq, Hkv, Hq / Hkv, D, width, splits, lsa::num_sms());
+    // the fixed arrays take the cluster / ticket plans only (the persistent plan's split
+    // partials can outgrow them)
+    lsa::ReadPlan p = lsa::plan_read(B * Tq, Hkv, Hq / Hkv, D, width, splits, lsa::num_sms(), false);
     if (p.scratch_bytes > lsa::kNoAllocScratchBytes || p.counters > lsa::kNoAllocCounters) return LSA_ERR_SIZE;
     lsa::NoAllocSlot slot;
     int rc = lsa::noalloc_setup(&slot);
@@ -912,7 +1279,7 @@ int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dty
         return LSA_ERR_CUDA;
     return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out,
                                    slot.scratch, lsa::kNoAllocScratchBytes, slot.counters, lsa::kNoAllocCounters,
-                                   splits, stream);
+                                   splits, stream, 0, nullptr, nullptr, false);
 }
 
 }  // extern "C"

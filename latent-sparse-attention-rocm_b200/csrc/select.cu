@@ -866,7 +866,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_finish_kernel(
 template <typename K>
 static int set_smem(K kernel, int bytes) {
     if (bytes > 48 * 1024) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess ||
+            cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared) != cudaSuccess)
             return LSA_ERR_CUDA;
     }
     return LSA_OK;

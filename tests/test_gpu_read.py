@@ -126,3 +126,52 @@ def test_read_rejects_cpu_and_bad_groups(lsa):
     with pytest.raises(AssertionError):
         lsa.read_kernel_tiled.sparse_read_auto(qg, kg, kg, torch.zeros(1, 1, 4, dtype=torch.int32, device=DEV),
                                                torch.zeros(1, 1, dtype=torch.int32, device=DEV))
+
+
+@pytest.mark.parametrize("dtype,B,Tq,hq,hkv,D,width", [
+    (torch.bfloat16, 40, 1, 64, 8, 128, 2112),  # batched decode rows: 320 (row, KV head) units
+    (torch.float16, 24, 3, 32, 8, 64, 1100),  # 576 units, D = 64, G = 4
+    (torch.bfloat16, 3, 100, 8, 2, 128, 700),  # prefill-like rows: 600 units, G = 4
+])
+def test_persistent_read_vs_oracle(oracle, lsa, dtype, B, Tq, hq, hkv, D, width):
+    """Batches with at least two (row, KV head) units per SM take the persistent read (16-bit
+    inputs; fp32 keeps the split kernel with ticket merges): ragged lengths (zero, partial,
+    full), -1 pads, out-of-range ids and duplicates, against the oracle."""
+    rng = np.random.default_rng(B * 31 + Tq)
+    Tk = 4096
+    ids = rng.integers(-1, Tk + 3, (B, Tq, width)).astype(np.int32)  # -1 pads and ids >= Tk are skipped
+    ids[..., 5:9] = ids[..., 1:5]  # duplicates count per occurrence
+    lengths = rng.integers(0, width + 1, (B, Tq)).astype(np.int32)
+    lengths.flat[0] = 0
+    lengths.flat[-1] = width
+    ids_ok = np.where((ids >= 0) & (ids < Tk), ids, -1).astype(np.int32)  # the checker's view of skipped ids
+    tq, tk, tv, _, ln, want = _case(oracle, B, Tq, Tk, hq, hkv, D, width, dtype, B + Tq, lengths=lengths, ids=ids_ok)
+    got = lsa.read_kernel_tiled.sparse_read_auto(tq, tk, tv, torch.from_numpy(ids).to(DEV), ln, D ** -0.5)
+    _check(got, want, dtype)
+    if dtype == torch.bfloat16:  # the fp32 inputs of the same case: split kernel, ticket merges
+        f = lambda x: x.float()
+        _check(lsa.read_kernel_tiled.sparse_read_auto(f(tq), f(tk), f(tv), torch.from_numpy(ids).to(DEV), ln,
+                                                      D ** -0.5), want, torch.bfloat16)
+
+
+def test_persistent_partial_reads_merge_to_full(lsa):
+    """Partial reads (fp32 output + log2-sum-exp, global ids with an id base) over two halves
+    of the keys, each through the persistent kernel, merge to the full read."""
+    from lsa_b200 import seqshard
+
+    g = torch.Generator(device=DEV)
+    g.manual_seed(5)
+    B, Hq, Hkv, D, Tk, width = 48, 32, 8, 128, 2048, 1500
+    q = torch.randn(B, 1, Hq, D, generator=g, device=DEV).to(torch.bfloat16)
+    k = torch.randn(B, Tk, Hkv, D, generator=g, device=DEV).to(torch.bfloat16)
+    v = torch.randn(B, Tk, Hkv, D, generator=g, device=DEV).to(torch.bfloat16)
+    ids = torch.randint(0, Tk, (B, 1, width), generator=g, device=DEV, dtype=torch.int32)
+    lens = torch.randint(0, width + 1, (B, 1), generator=g, device=DEV, dtype=torch.int32)
+    full = lsa.read_kernel_tiled.sparse_read_auto(q, k, v, ids, lens, D ** -0.5).float()
+    half = Tk // 2
+    parts = [seqshard.shard_partial_read(q, k[:, lo:lo + half].contiguous(), v[:, lo:lo + half].contiguous(), ids,
+                                         lens, lo, D ** -0.5) for lo in (0, half)]
+    outs = torch.stack([p[0] for p in parts])
+    lses = torch.stack([p[1] for p in parts])
+    merged = seqshard.merge_partials(outs.reshape(2, -1, D), lses.reshape(2, -1), torch.float32, q.shape)
+    assert float((merged - full).abs().max()) <= 2e-2
