@@ -601,9 +601,9 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
 
 // ------------------------------------------------------------------ persistent read
 
-// Bandwidth-bound batches (many (row, KV head) units, 16-bit inputs): a persistent grid of
-// one CTA per SM takes work items = (row, split, KV head) from a global queue (atomic
-// counter: SMs that run slower take fewer items). Four producer warps feed a ring of three
+// Bandwidth-bound batches (at least one (row, KV head) unit per SM, 16-bit inputs): a
+// persistent grid of one CTA per SM takes work items = (row, split, KV head) from a global
+// queue (atomic counter: SMs that run slower take fewer items). Four producer warps feed a ring of three
 // 128-id stages with 16-byte cp.async row pieces (full / empty mbarriers) while eight
 // consumer warps run the tensor-core stage, so the copy issue never waits behind the math
 // (measured: 256-byte TMA bulk copies per row issue too slowly for this - the SM takes one
@@ -940,7 +940,7 @@ static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t 
                           bool allow_persist = true) {
     ReadPlan p;
     int64_t units = R * Hkv;
-    if (splits_req <= 0 && allow_persist && units >= 2 * (int64_t)sms && width > 0 && (D == 64 || D == 128)) {
+    if (splits_req <= 0 && allow_persist && units >= (int64_t)sms && width > 0 && (D == 64 || D == 128)) {
         // bandwidth-bound batch: persistent grid (one CTA per SM), about four items per CTA
         // (measured best: more items balance better but each adds a split merge), at least
         // 512 ids per item; splits merge by ticket

@@ -121,3 +121,27 @@ def test_batched_select_wide_rows_stream_kernel(lsa, Hkv, D, bucket, cap, top_p,
         finally:
             os.environ.pop("LSA_SELECT_IMPL", None)
     assert int(gn[2]) == 64 + 4  # shorter than a block: window + sinks only
+
+
+def test_batched_select_narrow_rows_wide_batch(lsa):
+    """Rows that each fit one cluster but, together, enough columns to fill the GPU (at least
+    8192 row-columns) take the streaming scorer too: every row equals the reference arm of
+    flat_select on its own sequence."""
+    from lsa_b200 import batched
+
+    cfg = lsa.PortConfig(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap=128, top_p=32, top_k=2048,
+                         window_size=64, sink_size=4)
+    rng = np.random.default_rng(77)
+    lengths = [int(x) for x in rng.integers(12000, 16385, 40)]
+    lengths[3] = 200  # shorter than a block
+    q, k, v, iq, pos, per_seq = _case(lsa, lengths, 4, 2, 64, cfg, 31)
+    bb = batched.concat_buckets(per_seq)
+    assert len(lengths) * bb.max_rows >= 8192 and bb.max_rows <= 1024
+    gl, gn = batched.batched_select(iq, pos, bb, cfg)
+    os.environ["LSA_SELECT_IMPL"] = "reference"
+    try:
+        for b in range(len(lengths)):
+            wl, wn = lsa.flat_select(iq[b:b + 1], pos[b:b + 1], per_seq[b], cfg)
+            assert torch.equal(gl[b:b + 1], wl) and torch.equal(gn[b:b + 1], wn), b
+    finally:
+        os.environ.pop("LSA_SELECT_IMPL", None)
