@@ -273,6 +273,19 @@ int lsa_sparse_read_partial(const void* q, const void* k, const void* v, int dty
 int lsa_merge_partials(const float* o, const float* lse, int64_t P, int64_t n, int64_t D, int dtype, void* out,
                        cudaStream_t stream);
 
+/* ---------------------------------------------------------------- paged KV cache */
+
+/* The expansion walk's MAP_SLOTS path (select_fused.py:147-148, 177-199) as a pass over
+ * finished read lists: out[r, j] = slot_table[slot_rows[r], lists[r, j]] for j < lengths[r]
+ * (walked members, window and sinks alike), -1 past the length or for positions outside
+ * [0, table_cols) or a slot row outside [0, table_rows). slot_table [table_rows, ld_table]
+ * int32 maps each sequence's positions to physical slots of a KV pool; reading the mapped
+ * lists over the pool (k/v [1, slots, Hkv, D], one list row per query row) equals reading
+ * the position lists over each sequence's own cache. R <= 65535. */
+int lsa_map_slots(const int32_t* lists, const int32_t* lengths, int64_t R, int64_t width, const int32_t* slot_table,
+                  int64_t table_rows, int64_t table_cols, int64_t ld_table, const int32_t* slot_rows, int32_t* out,
+                  cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -232,3 +232,13 @@ def test_positional_picks_pattern(oracle):
     for row, v in ((p[2], 40), (p[3], 504)):
         assert row.size == 32 and (np.diff(row) > 0).all() and (row >= 0).all()
         assert list(row[:4]) == [0, 1, 2, 3] and list(row[-4:]) == [v - 4, v - 3, v - 2, v - 1]
+
+
+def test_oracle_map_slots_semantics(oracle):
+    """The MAP_SLOTS restatement: mapped entries below the length, -1 elsewhere, -1 for ids
+    outside the table and for slot rows outside it."""
+    table = np.array([[10, 11, 12, 13], [20, 21, 22, 23]], np.int32)
+    lists = np.array([[0, 3, 2, -1, 1], [3, 9, 0, 1, 2], [0, 1, 2, 3, 0]], np.int32)
+    lengths = np.array([4, 3, 5], np.int32)
+    got = oracle.map_slots(lists, lengths, table, np.array([1, 0, 5], np.int32))
+    assert got.tolist() == [[20, 23, 22, -1, -1], [13, -1, 10, -1, -1], [-1, -1, -1, -1, -1]]
