@@ -288,6 +288,7 @@ def run_b200(args, rank, world, dev):
 
     e2e_ms, us_dense, us_tree, us_positional = float("nan"), float("nan"), float("nan"), float("nan")
     ms_batch = float("nan")
+    index_maint = None
     if not args.quick:
         with torch.cuda.stream(stream):
             for _ in range(3):
@@ -353,6 +354,48 @@ def run_b200(args, rank, world, dev):
         ms_batch = timed(bgraph) / args.steps
         del kb, vb, bgraph
 
+        # index maintenance on layer 0's keys: a decode appends one position per step and a
+        # cluster block closes every 512 of them; the incremental index builds only that block
+        # (and any node block it completes) - against the full rebuild of the 32k index
+        from lsa_b200.incremental import IndexState
+        from lsa_b200.index_space import index_keys
+
+        ik0 = index_keys(layers[0]["k"][0])
+        blk = CFG["cluster_block_size"]
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            st_ix = IndexState(ik0.shape[1], pcfg, dev)
+            at = T_CTX - 4 * blk
+            st_ix.append(ik0[:at])
+            close_us, open_us = [], []
+            for _ in range(4):  # four block closes: positions up to the close, then the closing one
+                stream.synchronize()
+                ev0.record(stream)
+                for i in range(at, at + blk - 1):
+                    st_ix.append(ik0[i:i + 1])
+                ev1.record(stream)
+                stream.synchronize()
+                open_us.append(ev0.elapsed_time(ev1) * 1e3 / (blk - 1))
+                ev0.record(stream)
+                st_ix.append(ik0[at + blk - 1:at + blk])
+                ev1.record(stream)
+                stream.synchronize()
+                close_us.append(ev0.elapsed_time(ev1) * 1e3)
+                at += blk
+            ev0.record(stream)
+            for _ in range(3):
+                fb = lsa.build_buckets_gpu(ik0, pcfg)
+                lsa.build_hierarchy_gpu(ik0, fb, pcfg)
+            ev1.record(stream)
+            stream.synchronize()
+            us_rebuild = ev0.elapsed_time(ev1) / 3 * 1e3
+        index_maint = {"us_per_block_close": round(sorted(close_us)[len(close_us) // 2], 1),
+                       "us_per_open_append": round(sorted(open_us)[len(open_us) // 2], 2),
+                       "us_full_rebuild_32k": round(us_rebuild, 1), "block_closes": len(close_us),
+                       "note": "host-driven eager appends on layer 0's keys; a close builds one 512-position "
+                               "block (and any node block it completes)"}
+        del ik0, st_ix
+
     hbm, tflops, peak_kind = _load_peaks()
     read_gbs = read_bytes_per_launch / (us_read * 1e-6) / 1e9
     fused_impl = args.decode_impl != "split"
@@ -386,6 +429,7 @@ def run_b200(args, rank, world, dev):
             "sequences": LAYERS, "us_per_batch": round(ms_batch * 1e3, 2), "gbs": round(step_bytes / (ms_batch * 1e-3) / 1e9, 1),
             "hbm_frac": round(step_bytes / (ms_batch * 1e-3) / 1e9 / hbm, 4),
             "note": "the LAYERS caches decoded as one batch (batched select + batched read)"},
+        "index_maintenance": index_maint,
         "arms_us_per_decode": None if us_tree != us_tree else {
             "flat": round(ms_split / args.steps / LAYERS * 1e3, 3), "tree": round(us_tree, 3),
             "positional": round(us_positional, 3), "dense": round(us_dense, 3)},

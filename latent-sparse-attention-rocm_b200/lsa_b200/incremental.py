@@ -10,7 +10,7 @@ depends only on its ``node_cluster_block_size`` rows of the level below. So an a
 closes blocks only builds those blocks:
 
 * positions arrive with their index keys (``IndexState.append``); keys of the open block wait
-  in a buffer;
+  in a block-sized buffer;
 * every block that closes is built alone (``lsa_build_buckets`` over its keys, members
   offset by its start) and its buckets are appended;
 * every node block that completes at any level is paired alone (``lsa_pair_to_size``,
@@ -59,7 +59,8 @@ class IndexState:
         cap = config.bucket_cap
         self.positions = 0  # positions appended
         self.closed = 0  # positions covered by closed blocks
-        self._pending = torch.empty(0, d, dtype=torch.float32, device=self.device)  # keys of the open block
+        self._pend = torch.empty(config.cluster_block_size, d, dtype=torch.float32, device=self.device)
+        self._npend = 0  # keys of the open block, at the front of _pend
         self._cf = _Rows((d,), torch.float32, self.device)
         self._cb = _Rows((d,), torch.bfloat16, self.device)
         self._members = _Rows((cap,), torch.int32, self.device)
@@ -86,17 +87,31 @@ class IndexState:
     # ---------------------------------------------------------------- appends
 
     def append(self, index_keys: torch.Tensor) -> int:
-        """Append the index keys [n, d] of the next n positions; returns the buckets added."""
+        """Append the index keys [n, d] of the next n positions; returns the buckets added.
+
+        Keys of the open block are copied into a block-sized buffer (one copy per call); a
+        block closes as soon as its last key arrives."""
         pipeline.require_cuda(index_keys, what="IndexState.append")
         keys = index_keys.float().reshape(-1, self.d)
-        self.positions += keys.shape[0]
-        pending = torch.cat([self._pending, keys]) if self._pending.shape[0] else keys
+        n = keys.shape[0]
+        self.positions += n
         block = self.config.cluster_block_size
-        whole = pending.shape[0] // block * block
-        added = 0
+        i, added = 0, 0
+        if self._npend:  # complete the open block first
+            take = min(block - self._npend, n)
+            self._pend[self._npend:self._npend + take] = keys[:take]
+            self._npend += take
+            i = take
+            if self._npend == block:
+                added += self._close_blocks(self._pend)
+                self._npend = 0
+        whole = (n - i) // block * block  # whole blocks straight from the input
         if whole:
-            added = self._close_blocks(pending[:whole].contiguous())
-        self._pending = pending[whole:].clone()
+            added += self._close_blocks(keys[i:i + whole].contiguous())
+            i += whole
+        if i < n:  # the start of the next open block
+            self._pend[: n - i] = keys[i:]
+            self._npend = n - i
         return added
 
     def _close_blocks(self, keys: torch.Tensor) -> int:
