@@ -110,18 +110,23 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def _traffic_from_profile(name: str):
-    """dram bytes per launch recorded in the committed ncu summary (profiles/), else None."""
+def _profile_field(name: str, field: str):
+    """A `field: value` number recorded in the committed ncu summary (profiles/), else None."""
     p = ROOT / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(field + ":"):
             try:
                 return float(line.split(":", 1)[1].strip())
             except ValueError:
                 return None
     return None
+
+
+def _traffic_from_profile(name: str):
+    """dram bytes per launch recorded in the committed ncu summary (profiles/), else None."""
+    return _profile_field(name, "traffic_bytes_per_launch")
 
 
 # --------------------------------------------------------------------------- B200 arm
@@ -551,13 +556,14 @@ def run_batched(args, rank, world, dev):
     from lsa_b200 import batched
     from lsa_b200.index_space import index_keys, index_queries
 
-    B, HQB = 64, 64
+    B, HQB = args.batched_seqs, 64
+    len_lo, len_hi = (int(x) for x in args.batched_len.split(","))
     by_heads = args.batched_shard == "heads"
     if by_heads and HKV % world:
         raise ValueError(f"head sharding needs {HKV} KV heads to divide over {world} ranks")
     gen = torch.Generator(device="cpu")
     gen.manual_seed(SEED + 4)
-    lengths_all = torch.randint(65536, 131073, (B,), generator=gen).tolist()
+    lengths_all = torch.randint(len_lo, len_hi + 1, (B,), generator=gen).tolist()
     start, end = (0, B) if by_heads else batched.shard_rows(B, world, rank)
     lengths = lengths_all[start:end]
     h0, h1 = (rank * HKV // world, (rank + 1) * HKV // world) if by_heads else (0, HKV)
@@ -650,21 +656,36 @@ def run_batched(args, rank, world, dev):
         all_bytes, all_seqs = float(step_bytes), nb
     hbm, tflops, peak_kind = _load_peaks()
     value = all_bytes / (ms * 1e-3) / 1e9
+    # the dominant kernel: the read (persistent grid from one (row, KV head) unit per SM)
+    read_bytes = n_ids * hkv_r * DH * 2 * 2 + nb * hkv_r * G * DH * 2 * 2 + n_ids * 4
+    persist = nb * hkv_r >= torch.cuda.get_device_properties(dev).multi_processor_count
+    read_gbs = read_bytes / (us_read * 1e-6) / 1e9
+    prof = _traffic_from_profile("sparse_read_persist_batched.md")
+    traffic = None
+    if prof is not None and persist:  # the profiled launch's DRAM bytes per algorithmic byte, at this size
+        ratio = _profile_field("sparse_read_persist_batched.md", "traffic_per_algorithmic_byte")
+        traffic = round(read_bytes * ratio) if ratio else None
+    roof = {"bound": "hbm", "kernel": "lsa::sparse_read_persist_kernel" if persist else "lsa::sparse_read_kernel",
+            "achieved": round(read_gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(read_gbs / hbm, 4),
+            "peak_kind": peak_kind, "traffic": traffic, "bytes_per_launch": int(read_bytes)}
     return {
-        "metric": "batched decode select+read GB/s @128k bf16 (64 sequences)", "value": round(value, 2),
+        "metric": f"batched decode select+read GB/s @128k bf16 ({B} sequences)", "value": round(value, 2),
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) q/k/v, lengths U[65536, 131072])",
+        "data": f"synthetic (seeded N(0,1) q/k/v, lengths U[{len_lo}, {len_hi}])",
         "config": {"workload": "batched128k", "batch": B, "sequences_per_rank": nb, "heads_q": HQB,
                    "heads_kv": HKV, "heads_kv_per_rank": hkv_r, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
                    "budget_tokens": BATCH_CFG["top_k"],
+                   "lengths": [len_lo, len_hi],
                    "parallelism": f"{'kv-head' if by_heads else 'sequence'}-shard{world}",
                    "l2": "no flush: one step reads > 1 GB of K/V"},
         "us_per_step": round(ms * 1e3, 2), "us_select": round(us_select, 2), "us_read": round(us_read, 2),
         "sequences": all_seqs, "bytes_per_step": int(all_bytes),
         # per step: the read, and the selection - one launch, or two (streaming scorer + per-row
         # finish) when the widest row has more than 1024 buckets (more than one cluster)
-        "gpu_launches": args.steps * (1 + (2 if bb.max_rows > 1024 else 1)), "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
+        "roofline": roof,
+        "gpu_launches": args.steps * (1 + (2 if bb.max_rows > 1024 or nb * bb.max_rows >= 8192 else 1)),
+        "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
         "clocks": clocks.summary(),
     }
 
@@ -910,6 +931,9 @@ def main() -> int:
     parser.add_argument("--tree-ctx", type=int, default=1 << 20, help="tree1m context length")
     parser.add_argument("--decode-impl", default="split", choices=["split", "fused"],
                         help="decode32k step: the select and read launches (default), or one fused launch")
+    parser.add_argument("--batched-seqs", type=int, default=64, help="batched128k sequences (profiling: fewer)")
+    parser.add_argument("--batched-len", default="65536,131072",
+                        help="batched128k sequence length range min,max (profiling: shorter)")
     parser.add_argument("--batched-shard", default="heads", choices=["heads", "sequences"],
                         help="batched128k over ranks: by KV head (selection replicated) or by sequence")
     args = parser.parse_args()

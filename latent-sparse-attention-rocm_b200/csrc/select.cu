@@ -656,8 +656,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
 // launches. (1) select_stream_kernel, a persistent grid, streams the centroid tables
 // through shared memory with TMA bulk copies while scoring warps consume them, so HBM sees
 // one continuous stream per SM:
-//   * work items: 128 visible columns of one row; CTA b takes items b, b + grid, ... in
-//     row order;
+//   * work items: item_cols (<= 128, a multiple of a stage's columns) visible columns of
+//     one row - smaller items when the batch is small, so every CTA gets work; CTA b takes
+//     items b, b + grid, ... in row order;
 //   * one producer warp (lane 0) copies 32 KB stages (contiguous centroid rows) into a ring
 //     of kStreamStages buffers (full/empty mbarriers, bounded waits) and posts each stage's
 //     (row, first column, columns) beside it;
@@ -671,7 +672,7 @@ constexpr int kStreamWarps = 8;
 constexpr int kStreamThreads = 32 * (kStreamWarps + 1);
 constexpr int kStreamStages = 3;
 constexpr int kStreamStageBytes = 32768;
-constexpr int kStreamItemCols = 128;
+constexpr int kStreamItemCols = 128;  // the largest work item (columns of one row)
 constexpr int kStreamMaxRows = 256;
 constexpr int kFinishMaxTopK = 16384;  // read-list slots gathered in shared memory
 
@@ -690,7 +691,7 @@ __device__ __forceinline__ int64_t stream_visible(const RowPos& rp, int r, int64
 template <typename TQ, int CHUNKS>
 __global__ void __launch_bounds__(kStreamThreads, 2) select_stream_kernel(
     const TQ* __restrict__ q, int64_t ldq, const __nv_bfloat16* __restrict__ c, int64_t N, int d, RowPos rp,
-    int64_t block, int64_t bpb, int R, int64_t* __restrict__ ws_keys, int32_t* __restrict__ status) {
+    int64_t block, int64_t bpb, int R, int item_cols, int64_t* __restrict__ ws_keys, int32_t* __restrict__ status) {
     constexpr int NS = kStreamStages;
     extern __shared__ __align__(128) unsigned char stage_buf[];  // [NS][32 KB]
     __shared__ __align__(8) uint64_t full[NS], empty[NS];
@@ -721,7 +722,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) select_stream_kernel(
             if (r < R) {
                 const int64_t cnt = stream_visible(rp, r, N, block, bpb);
                 row_count[r] = (int)cnt;
-                n_items[i] = (int)((cnt + kStreamItemCols - 1) / kStreamItemCols);
+                n_items[i] = (int)((cnt + item_cols - 1) / item_cols);
             }
             mine += n_items[i];
         }
@@ -759,8 +760,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) select_stream_kernel(
                         else hi = mid - 1;
                     }
                     r = lo;
-                    col0 = (it - item_start[r]) * kStreamItemCols;
-                    col1 = min(col0 + kStreamItemCols, row_count[r]);
+                    col0 = (it - item_start[r]) * item_cols;
+                    col1 = min(col0 + item_cols, row_count[r]);
                 }
                 for (int c0 = col0;; c0 += cps) {  // a stop posts one stage with row -1
                     const int slot = s % NS;
@@ -1056,7 +1057,16 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     if (!many_rows && (!use_cluster || wide_batch) && c_dtype == kBF16 && (q_dtype == kBF16 || q_dtype == kF32) &&
         R <= kStreamMaxRows && top_p <= 128 && k * cap <= kMemberPrefetch && cap % 4 == 0 && aligned16(members) &&
         top_k <= kFinishMaxTopK && n_counters >= R + 1 && d * 2 <= kStreamStageBytes && N < (1ll << 30)) {
-        int64_t items = R * ((most + kStreamItemCols - 1) / kStreamItemCols);
+        // item size: up to 128 columns, smaller (whole stages) until the batch makes about two
+        // items per CTA slot
+        const int cps_host = (int)(kStreamStageBytes / (d * 2));
+        const int64_t slots_host = 2 * (int64_t)num_sms_select();
+        int64_t icols = R * most / (2 * slots_host);
+        if (icols > kStreamItemCols) icols = kStreamItemCols;
+        icols = icols / cps_host * cps_host;
+        if (icols < cps_host) icols = cps_host;
+        const int item_cols = (int)icols;
+        int64_t items = R * ((most + item_cols - 1) / item_cols);
         if (items < 1) items = 1;
 #define LSA_ST(TQ, CH)                                                                                              \
     do {                                                                                                            \
@@ -1077,7 +1087,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
         sc.attrs = &pdl;                                                                                            \
         sc.numAttrs = 1;                                                                                            \
         if (cudaLaunchKernelEx(&sc, kern, (const TQ*)queries, ldq, (const __nv_bfloat16*)centroids, N, (int)d,     \
-                               positions, block, bpb, (int)R, ws_keys, counters + R) != cudaSuccess)                \
+                               positions, block, bpb, (int)R, item_cols, ws_keys, counters + R) != cudaSuccess)     \
             return LSA_ERR_CUDA;                                                                                    \
     } while (0)
 #define LSA_FIN(KW)                                                                                                 \
