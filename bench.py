@@ -741,23 +741,43 @@ def run_tree1m(args, rank, world, dev):
     pos = torch.full((1,), C - 1, dtype=torch.int32, device=dev)
     scale = DH ** -0.5
 
-    def step():
-        return [seqshard.seqshard_decode(q[b:b + 1], k[b:b + 1], v[b:b + 1], iq[b], pos, shards[b], pcfg, gather,
-                                         scale) for b in range(B)]
+    qs, ks, vs = [q[b:b + 1] for b in range(B)], [k[b:b + 1] for b in range(B)], [v[b:b + 1] for b in range(B)]
+
+    def step():  # all sequences' candidates in one all-gather, all partials in a second
+        return seqshard.seqshard_decode_batch(qs, ks, vs, iq, pos, shards, pcfg, gather, scale)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
+    # one step captured in a CUDA graph (the step is a chain of small launches: replaying it
+    # removes the host's launch overhead); with several ranks the graph holds the NCCL
+    # all-gathers too, which needs --tree-graph-nccl (off by default)
+    use_graph = not args.tree_eager and (world == 1 or args.tree_graph_nccl)
+    graph = None
+    if use_graph:
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            step()
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+        torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clocks:
         ev0.record()
         for _ in range(args.steps):
-            step()
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
         ev1.record()
         torch.cuda.synchronize(dev)
     ms = ev0.elapsed_time(ev1) / args.steps
+    del graph  # a graph holding NCCL calls goes before the process group does
     if world > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -777,7 +797,8 @@ def run_tree1m(args, rank, world, dev):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded drift keys, N(0,1) q/v)",
         "config": {"workload": "tree1m", "batch": B, "context": C, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
-                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": "NCCL all-gather x3/seq",
+                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": "NCCL all-gather x2/step (candidates, partials)",
+                   "cuda_graph": use_graph,
                    **{k2: TREE_CFG[k2] for k2 in ("bucket_size", "top_p", "top_k", "beam_width")},
                    "l2": "no flush: 4 x 1M-token caches (16 GiB) >> L2"},
         "effective_gbs": round(value, 2), "step_roofline_frac": round(value / world / hbm, 4),
@@ -929,6 +950,9 @@ def main() -> int:
                         help="decode32k (default: + prefill leg), the 64-sequence 128k batched decode, or the "
                              "sequence-sharded 1M tree decode")
     parser.add_argument("--tree-ctx", type=int, default=1 << 20, help="tree1m context length")
+    parser.add_argument("--tree-eager", action="store_true", help="tree1m: time eager launches, no CUDA graph")
+    parser.add_argument("--tree-graph-nccl", action="store_true",
+                        help="tree1m with several ranks: capture the NCCL all-gathers in the step's CUDA graph")
     parser.add_argument("--decode-impl", default="split", choices=["split", "fused"],
                         help="decode32k step: the select and read launches (default), or one fused launch")
     parser.add_argument("--batched-seqs", type=int, default=64, help="batched128k sequences (profiling: fewer)")

@@ -372,7 +372,7 @@ int64_t r256(int64_t x) { return (x + 255) / 256 * 256; }
 template <typename T, int G>
 int occupancy_blocks(int smem) {
     int per_sm = 0;
-    if (smem > 48 * 1024 && cudaFuncSetAttribute(fused_decode_kernel<T, G>,
+    if (smem > 40 * 1024 && cudaFuncSetAttribute(fused_decode_kernel<T, G>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_decode_kernel<T, G>, kDecThreads, smem) !=
@@ -503,7 +503,7 @@ int lsa_decode_fused(const void* index_queries, int64_t R, int64_t ldq, const vo
 #define LSA_DEC_LAUNCH(TT, GG)                                                                                \
     do {                                                                                                    \
         auto kern = fused_decode_kernel<TT, GG>;                                                            \
-        if (p.smem > 48 * 1024 &&                                                                           \
+        if (p.smem > 40 * 1024 &&                                                                           \
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem) != cudaSuccess) \
             return LSA_ERR_CUDA;                                                                            \
         e = cudaLaunchCooperativeKernel((const void*)kern, dim3(p.grid), dim3(kDecThreads), args, p.smem,   \

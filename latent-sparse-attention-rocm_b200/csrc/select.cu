@@ -448,6 +448,50 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
                                (int)threadIdx.x, BlockSync{});
 }
 
+// The same walk with every picked member row staged in shared memory first (16-byte
+// cp.async pieces when cap % 4 == 0 and the table is 16-byte aligned, else plain loads):
+// one memory round trip instead of two per 2048-slot tile, then expand_walk with its output
+// gathered in shared memory. Dynamic smem: round4(P * cap) + top_k ints.
+template <typename PickT>
+__global__ void __launch_bounds__(512) expand_staged_kernel(const PickT* __restrict__ picks, int P, int64_t ldp,
+                                                            const int32_t* __restrict__ members, int64_t member_rows,
+                                                            int cap, const int32_t* __restrict__ positions, int window,
+                                                            int sink, int top_k, int32_t* __restrict__ lists,
+                                                            int32_t* __restrict__ lengths, int vec16) {
+    extern __shared__ __align__(16) int esm[];
+    __shared__ int scan_smem[33];
+    const int total = P * cap;
+    int* mem = esm;
+    int* gather = esm + ((total + 3) & ~3);
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const PickT* prow = picks + (int64_t)r * ldp;
+    auto bucket = [&](int p) -> int {
+        if constexpr (sizeof(PickT) == 8) return key_bucket((int64_t)prow[p]);
+        else return (int)prow[p];
+    };
+    if (vec16) {
+        const int q4 = cap / 4;
+        for (int i = tid; i < P * q4; i += blockDim.x) {
+            const int pk = i / q4, piece = i - pk * q4;
+            const int b = bucket(pk);
+            int* dst = mem + pk * cap + piece * 4;
+            if (b >= 0 && b < member_rows) cp_async16(smem_u32(dst), members + (int64_t)b * cap + piece * 4, 16);
+            else *reinterpret_cast<int4*>(dst) = make_int4(-1, -1, -1, -1);
+        }
+        cp_async_wait_all();
+    } else {
+        for (int s = tid; s < total; s += blockDim.x) {
+            const int pk = s / cap, m = s - pk * cap;
+            const int b = bucket(pk);
+            mem[s] = (b >= 0 && b < member_rows) ? members[(int64_t)b * cap + m] : -1;
+        }
+    }
+    __syncthreads();
+    const int width = top_k + window + sink;
+    expand_walk<512>(mem, total, positions[r], window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
+                     scan_smem, tid, BlockSync{}, gather);
+}
+
 // One launch from index queries to read lists. grid = (chunks, R), block = 512: every
 // warp scores one visible column; the last CTA of a row (atomic ticket) orders the row's
 // packed keys (register bitonic up to 512 keys) and walks the expansion.
@@ -866,7 +910,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_finish_kernel(
 
 template <typename K>
 static int set_smem(K kernel, int bytes) {
-    if (bytes > 48 * 1024) {
+    // opt in above 40 KB of dynamic memory: the kernel's static shared memory counts toward
+    // the 48 KB default too
+    if (bytes > 40 * 1024) {
         if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess ||
             cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared) != cudaSuccess)
@@ -905,6 +951,11 @@ static int launch_scores(const void* q, int64_t R, int64_t ldq, const void* c, i
 using namespace lsa;
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// the expansion launch (defined with the other launchers below)
+static int expand_launch(bool keys64, const void* picks, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
+                         int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                         int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream);
 
 static int num_sms_select() {
     int dev = 0, n = 148;
@@ -979,11 +1030,8 @@ int lsa_expand_in_order(const int32_t* picked, int64_t R, int64_t P, int64_t ldp
                         int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
     if (cap <= 0 || window < 0 || sink < 0 || top_k < 0 || P < 0) return LSA_ERR_ARG;
     if (R == 0) return LSA_OK;
-    expand_kernel<int32_t><<<(unsigned)R, 512, 0, stream>>>(picked, (int)P, ldp, members, member_rows, (int)cap,
-                                                           positions, (int)window, (int)sink, (int)top_k, lists,
-                                                           lengths);
-    LSA_LAUNCH_CHECK();
-    return LSA_OK;
+    return expand_launch(false, picked, R, P, ldp, members, member_rows, cap, positions, window, sink, top_k, lists,
+                         lengths, stream);
 }
 
 int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk, const int32_t* members,
@@ -991,11 +1039,8 @@ int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk,
                          int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
     if (cap <= 0 || window < 0 || sink < 0 || top_k < 0 || P < 0) return LSA_ERR_ARG;
     if (R == 0) return LSA_OK;
-    expand_kernel<int64_t><<<(unsigned)R, 512, 0, stream>>>(keys, (int)P, ldk, members, member_rows, (int)cap,
-                                                           positions, (int)window, (int)sink, (int)top_k, lists,
-                                                           lengths);
-    LSA_LAUNCH_CHECK();
-    return LSA_OK;
+    return expand_launch(true, keys, R, P, ldk, members, member_rows, cap, positions, window, sink, top_k, lists,
+                         lengths, stream);
 }
 
 // Scratch of lsa_select_fused: the packed keys [R, N] int64. Counters: one int32 ticket
@@ -1003,6 +1048,40 @@ int lsa_expand_from_keys(const int64_t* keys, int64_t R, int64_t P, int64_t ldk,
 int64_t lsa_select_fused_scratch(int64_t R, int64_t N) { return ((R * N * 8 + 255) / 256) * 256; }
 
 }  // extern "C"
+
+// The expansion launch: member rows staged in shared memory when they (and the gathered
+// output) fit, else the tiled walk reading members from global memory.
+static int expand_launch(bool keys64, const void* picks, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
+                         int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                         int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
+    const int64_t staged = ((P * cap + 3) / 4 * 4 + top_k) * 4;
+    if (staged <= 200 * 1024 && P * cap < (1 << 30)) {
+        const int vec16 = cap % 4 == 0 && aligned16(members);
+        if (keys64) {
+            auto kern = expand_staged_kernel<int64_t>;
+            if (set_smem(kern, (int)staged)) return LSA_ERR_CUDA;
+            kern<<<(unsigned)R, 512, (size_t)staged, stream>>>((const int64_t*)picks, (int)P, ldp, members, member_rows,
+                                                              (int)cap, positions, (int)window, (int)sink, (int)top_k,
+                                                              lists, lengths, vec16);
+        } else {
+            auto kern = expand_staged_kernel<int32_t>;
+            if (set_smem(kern, (int)staged)) return LSA_ERR_CUDA;
+            kern<<<(unsigned)R, 512, (size_t)staged, stream>>>((const int32_t*)picks, (int)P, ldp, members, member_rows,
+                                                              (int)cap, positions, (int)window, (int)sink, (int)top_k,
+                                                              lists, lengths, vec16);
+        }
+    } else if (keys64) {
+        expand_kernel<int64_t><<<(unsigned)R, 512, 0, stream>>>((const int64_t*)picks, (int)P, ldp, members,
+                                                               member_rows, (int)cap, positions, (int)window,
+                                                               (int)sink, (int)top_k, lists, lengths);
+    } else {
+        expand_kernel<int32_t><<<(unsigned)R, 512, 0, stream>>>((const int32_t*)picks, (int)P, ldp, members,
+                                                               member_rows, (int)cap, positions, (int)window,
+                                                               (int)sink, (int)top_k, lists, lengths);
+    }
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
+}
 
 // The fused selection's launch for token rows and tile rows alike (RowPos).
 static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids,

@@ -14,9 +14,12 @@
 // descending - score first, the lower id on ties. Scores: canonical fp32 cdot.
 //
 // Launches: one per node level (top down) and one for level 0. Each launch scores its
-// candidates over a grid of CTAs; the last CTA of a row (atomic ticket) sorts the row's
-// keys and writes the next level's carried rows (or the picks).
+// candidates over a grid of CTAs (two candidates per warp, up to two CTAs per SM); the last
+// CTA of a row (atomic ticket) keeps the row's best keys - a warp-list top-K when the beam
+// / top_p is at most 128, else a full sort - and writes the next level's carried rows (or
+// the picks).
 #include "common.cuh"
+#include "topk.cuh"
 
 namespace lsa {
 
@@ -73,7 +76,19 @@ struct TreeLevelArgs {
     int32_t* status;
 };
 
-template <int CHUNKS>
+struct TreeCandKeys {
+    const int64_t* row;
+    int count;
+    __device__ int64_t operator()(int i) const { return i < count ? __ldcg(row + i) : kEmpty; }
+};
+
+struct TreeBlockSync {
+    __device__ __forceinline__ void operator()() const { __syncthreads(); }
+};
+
+// KW > 0: the last CTA keeps the best K = 32 KW keys by warp-list sorts and a merge tree
+// (keep <= K); KW == 0: it sorts every candidate (bitonic in shared memory).
+template <int CHUNKS, int KW>
 __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
     extern __shared__ int64_t tsm[];
     __shared__ int is_last;
@@ -130,22 +145,30 @@ __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
     __threadfence();
     // phase 2 (last CTA of the row): order the candidates, keep the best
     int kept = 0;
+    int64_t* best = tsm;  // the kept keys, best first
     if (active && n_cand > 0) {
-        int n2 = next_pow2(n_cand);
-        for (int i = threadIdx.x; i < n2; i += blockDim.x)
-            tsm[i] = i < n_cand ? __ldcg(a.ws_keys + (int64_t)r * a.cand_cap + i) : kEmpty;
-        __syncthreads();
-        bitonic_sort_desc(tsm, n2);
+        if constexpr (KW > 0) {
+            constexpr int K = 32 * KW;
+            best = tsm + 8 * K;
+            group_topk_desc<KW, 8>(TreeCandKeys{a.ws_keys + (int64_t)r * a.cand_cap, n_cand}, n_cand, tsm, best,
+                                   warp, lane, TreeBlockSync{});
+        } else {
+            int n2 = next_pow2(n_cand);
+            for (int i = threadIdx.x; i < n2; i += blockDim.x)
+                tsm[i] = i < n_cand ? __ldcg(a.ws_keys + (int64_t)r * a.cand_cap + i) : kEmpty;
+            __syncthreads();
+            bitonic_sort_desc(tsm, n2);
+        }
         kept = n_cand < a.keep ? n_cand : a.keep;
     }
     if (a.L == 0) {
         for (int i = threadIdx.x; i < a.keep; i += blockDim.x) {
-            a.picks[(int64_t)r * a.keep + i] = i < kept ? key_bucket(tsm[i]) : -1;
+            a.picks[(int64_t)r * a.keep + i] = i < kept ? key_bucket(best[i]) : -1;
             if (a.pick_keys) {  // same score bits, column rebased (e.g. to a global bucket id)
                 int64_t key = kEmpty;
                 if (i < kept) {
-                    const uint64_t hi = (uint64_t)tsm[i] & 0xFFFFFFFF00000000ull;
-                    key = (int64_t)(hi | (uint32_t)(0x7FFFFFFF - (key_bucket(tsm[i]) + (int32_t)a.col_offset)));
+                    const uint64_t hi = (uint64_t)best[i] & 0xFFFFFFFF00000000ull;
+                    key = (int64_t)(hi | (uint32_t)(0x7FFFFFFF - (key_bucket(best[i]) + (int32_t)a.col_offset)));
                 }
                 a.pick_keys[(int64_t)r * a.keep + i] = key;
             }
@@ -153,7 +176,7 @@ __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
     } else {
         int S = (int)a.size;
         for (int i = threadIdx.x; i < kept * S; i += blockDim.x) {
-            int node = key_bucket(tsm[i / S]);
+            int node = key_bucket(best[i / S]);
             a.carried_out[(int64_t)r * a.carry_cap + i] = (int32_t)a.children[(int64_t)node * S + (i % S)];
         }
         if (threadIdx.x == 0) a.carried_n_out[r] = active ? kept * S : 0;
@@ -253,6 +276,11 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
     int chunks = (int)((d / 8 + 31) / 32);
     int smem = next_pow2(p.cand_cap) * 8;
     if (smem < 1024) smem = 1024;
+    int sms = 148;
+    {
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    }
     int cur = 0;
     for (int64_t L = n_built; L >= 0; --L) {
         a.L = (int)L;
@@ -265,23 +293,35 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
         a.carried_n_out = carry_n[cur ^ 1];
         int64_t bound = L > 0 ? (level_counts[L - 1] > p.carry_cap + nb ? level_counts[L - 1] : p.carry_cap + nb)
                               : p.cand_cap;
-        int64_t want = (bound + 63) / 64;  // 8 warps x 8 candidates per CTA
-        int64_t spread = (296 + R - 1) / R;  // about two CTAs per SM over all rows
+        int64_t want = (bound + 15) / 16;  // 8 warps x 2 candidates per CTA
+        int64_t spread = (2 * (int64_t)sms + R - 1) / R;  // about two CTAs per SM over all rows
         unsigned gx = (unsigned)(want < spread ? want : spread);
         if (gx < 1) gx = 1;
         dim3 grid(gx, (unsigned)R);
-#define LSA_TL(CH)                                                                                         \
-    do {                                                                                                   \
-        auto kern = tree_level_kernel<CH>;                                                                 \
-        if (smem > 48 * 1024 &&                                                                            \
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) \
-            return LSA_ERR_CUDA;                                                                           \
-        kern<<<grid, 256, smem, stream>>>(a);                                                              \
+        // the kept keys: warp-list top-K for keep <= 128 (K keys per warp, merge tree), else a
+        // full bitonic sort of the candidates
+        const int kw = a.keep <= 32 ? 1 : (a.keep <= 64 ? 2 : (a.keep <= 128 ? 4 : 0));
+        const int lsmem = kw ? 9 * 32 * kw * 8 : smem;
+#define LSA_TL(CH, KW)                                                                                      \
+    do {                                                                                                    \
+        auto kern = tree_level_kernel<CH, KW>;                                                              \
+        if (lsmem > 40 * 1024 &&                                                                            \
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, lsmem) != cudaSuccess) \
+            return LSA_ERR_CUDA;                                                                            \
+        kern<<<grid, 256, lsmem, stream>>>(a);                                                              \
     } while (0)
-        if (chunks <= 1) LSA_TL(1);
-        else if (chunks <= 2) LSA_TL(2);
-        else if (chunks <= 4) LSA_TL(4);
-        else LSA_TL(8);
+#define LSA_TL_KW(CH)                         \
+    do {                                      \
+        if (kw == 1) LSA_TL(CH, 1);           \
+        else if (kw == 2) LSA_TL(CH, 2);      \
+        else if (kw == 4) LSA_TL(CH, 4);      \
+        else LSA_TL(CH, 0);                   \
+    } while (0)
+        if (chunks <= 1) LSA_TL_KW(1);
+        else if (chunks <= 2) LSA_TL_KW(2);
+        else if (chunks <= 4) LSA_TL_KW(4);
+        else LSA_TL_KW(8);
+#undef LSA_TL_KW
 #undef LSA_TL
         LSA_LAUNCH_CHECK();
         cur ^= 1;

@@ -192,3 +192,30 @@ def seqshard_decode(q, k_shard, v_shard, index_queries, positions, s: ShardIndex
     outs, lses = gather(out), gather(lse)  # [world, R, Hq, D], [world, R, Hq]
     Hq, D = out.shape[1], out.shape[2]
     return merge_partials(outs.reshape(outs.shape[0], -1, D), lses.reshape(lses.shape[0], -1), q.dtype, q.shape)
+
+
+def seqshard_decode_batch(qs, ks, vs, index_queries, positions, shards, config, gather, scale=None):
+    """One decode step of several sharded sequences with TWO exchanges in all: the candidate
+    keys of every sequence in one all-gather, the partial outputs and log2-sum-exps of every
+    sequence in a second one, then one log-sum-exp merge over all of them.
+
+    qs[b] [1, R, Hq, D], this rank's ks[b] / vs[b] shard [1, length_b, Hkv, D], index_queries[b]
+    [R, d], shards[b] its ShardIndex; positions [R] shared. Returns [B, 1, R, Hq, D] in q's dtype,
+    equal to ``seqshard_decode`` sequence by sequence."""
+    B = len(shards)
+    keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config) for b in range(B)])
+    all_keys = gather(keys)  # [world, B, R, top_p]
+    R = keys.shape[1]
+    outs, lses = [], []
+    for b in range(B):
+        cand = all_keys[:, b].permute(1, 0, 2).reshape(R, -1)
+        lists, lengths = select_from_candidates(cand, positions, shards[b].members_global, config)
+        o, l = shard_partial_read(qs[b], ks[b], vs[b], lists[None], lengths[None], shards[b].start, scale)
+        outs.append(o)
+        lses.append(l)
+    D = outs[0].shape[-1]
+    packed = torch.cat([torch.stack(outs).reshape(-1, D), torch.stack(lses).reshape(-1, 1)], dim=1)  # [n, D + 1]
+    g = gather(packed)  # [world, n, D + 1]
+    q0 = qs[0]
+    merged = merge_partials(g[..., :D].contiguous(), g[..., D].contiguous(), q0.dtype, (B,) + tuple(q0.shape))
+    return merged

@@ -28,9 +28,14 @@ def test_header_declares_entry_points():
 def test_library_exports_every_declared_symbol():
     from lsa_b200 import _lib
 
+    undefined = subprocess.run(["nm", "-D", "--undefined-only", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    own = [ln for ln in undefined.stdout.splitlines() if "_ZN3lsa" in ln or " lsa_" in ln]
+    assert not own, f"the library references its own symbols that it does not define: {own}"
     try:
         L = _lib.lib()
     except OSError as e:  # a machine without the CUDA runtime cannot dlopen it
+        if "undefined symbol" in str(e):
+            raise
         pytest.skip(f"CUDA runtime not loadable here: {e}")
     for name in _declared():
         assert hasattr(L, name), name

@@ -100,3 +100,22 @@ def test_partial_read_lse_and_empty_shard(lsa):
                                      torch.stack([l_a, l_b]).reshape(2, -1), q.dtype, q.shape)
     ref = lsa.lsa_read(q, k, v, lists, lengths, 128 ** -0.5)
     assert float((merged.float() - ref.float()).abs().max()) <= 2e-2
+
+
+def test_batched_step_equals_per_sequence(lsa, oracle):
+    """The two-exchange step over several sequences (candidates of all sequences in one
+    gather, all partials in a second, one merge) equals the per-sequence step, here with one
+    rank (the gather adds the rank axis)."""
+    from lsa_b200 import seqshard
+
+    C = 16384
+    seqs = [_setup(lsa, oracle, C, 1, seed=s) for s in (21, 22, 23)]
+    pos = torch.tensor([C - 1], dtype=torch.int32, device=DEV)
+    gather = lambda x: x[None]
+    pcfg = seqs[0][4]
+    want = [seqshard.seqshard_decode(s[0], s[1], s[2], s[3], pos, s[6][0], pcfg, gather) for s in seqs]
+    got = seqshard.seqshard_decode_batch([s[0] for s in seqs], [s[1] for s in seqs], [s[2] for s in seqs],
+                                         [s[3] for s in seqs], pos, [s[6][0] for s in seqs], pcfg, gather)
+    assert got.shape == (3,) + tuple(seqs[0][0].shape)
+    for b in range(3):
+        assert torch.equal(got[b], want[b])
