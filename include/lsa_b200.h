@@ -286,6 +286,14 @@ int lsa_map_slots(const int32_t* lists, const int32_t* lengths, int64_t R, int64
                   int64_t table_rows, int64_t table_cols, int64_t ld_table, const int32_t* slot_rows, int32_t* out,
                   cudaStream_t stream);
 
+/* ---------------------------------------------------------------- self-test */
+
+/* The bounded wait every kernel uses (no reference counterpart): a one-thread kernel waits on
+ * an mbarrier of its own with the same helper. arrive != 0: the phase completes, *status = 0;
+ * arrive == 0: nothing arrives, the wait gives up after limit_ns (<= 2 s) and *status =
+ * LSA_ERR_TIMEOUT. Tests the failure path without a fault or a hang. */
+int lsa_wait_selftest(int32_t* status, int64_t limit_ns, int arrive, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

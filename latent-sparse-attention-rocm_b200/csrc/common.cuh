@@ -247,12 +247,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: true when the phase completed, false after ~2 s.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+// Bounded wait: true when the phase completed, false after limit_ns (default 2 s).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  uint64_t limit_ns = 2000000000ull) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = global_ns();
     while (!mbar_try_wait(bar, parity)) {
-        if (global_ns() - t0 > 2000000000ull) return false;
+        if (global_ns() - t0 > limit_ns) return false;
     }
     return true;
 }

@@ -59,6 +59,7 @@ SIGNATURES = {
                                   _P, _P, _I, _P, _I, _I, _P]),
     "lsa_decode_fused_plan": (_INT, [_I, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_map_slots": (_INT, [_P, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "lsa_wait_selftest": (_INT, [_P, _I, _INT, _P]),
     "lsa_decode_fused": (_INT, [_P, _I, _I, _P, _I, _I, _P, _I, _P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _INT, _I, _I,
                                 _I, _I, _F, _P, _P, _P, _P, _I, _P, _I, _P]),
     "lsa_tile_queries": (_INT, [_P, _INT, _I, _I, _I, _I, _P, _P]),
