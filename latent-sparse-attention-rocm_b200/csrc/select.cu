@@ -310,6 +310,7 @@ struct RowPos {
 
 constexpr int kFusedThreads = 512;
 constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
+constexpr int kGatherMax = 8192;       // read-list slots the fused selects gather in shared memory
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -415,11 +416,12 @@ struct BlockSync {
 // The walk of expand_row with every picked bucket's member row staged in shared memory
 // first (one memory round trip), then expand_walk over all (pick, member) slots. A block of
 // kFusedThreads threads. Requires P * cap <= kMemberPrefetch; mem (16-byte aligned) holds
-// that many int32.
+// that many int32; gather (optional, top_k int32) collects the kept ids for one coalesced
+// copy out.
 __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t* __restrict__ members,
                                       int64_t member_rows, int cap, int64_t pos, int window, int sink, int top_k,
                                       int32_t* __restrict__ out, int width, int32_t* length_out, int* scan_smem,
-                                      int* mem) {
+                                      int* mem, int* gather = nullptr) {
     const int total = P * cap;
     // addresses first, then every member load of this thread in flight together, then the
     // stores: one memory round trip for the whole staging
@@ -445,7 +447,7 @@ __device__ void expand_row_prefetched(const int64_t* picks, int P, const int32_t
     }
     __syncthreads();
     expand_walk<kFusedThreads>(mem, total, pos, window, sink, top_k, out, width, length_out, scan_smem,
-                               (int)threadIdx.x, BlockSync{});
+                               (int)threadIdx.x, BlockSync{}, gather);
 }
 
 // The same walk with every picked member row staged in shared memory first (16-byte
@@ -590,8 +592,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_fused_kernel(
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
         int* mem = reinterpret_cast<int*>(sbuf + ((k + 1) & ~1));  // 16-byte aligned
+        int* gather = top_k <= kGatherMax ? mem + (k * cap + 3) / 4 * 4 : nullptr;
         expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
-                              lengths + r, scan_smem, mem);
+                              lengths + r, scan_smem, mem, gather);
     } else {
         SmemPicks pk{picks};
         expand_row(pk, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
@@ -683,8 +686,9 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     int width = top_k + window + sink;
     if (k * cap <= kMemberPrefetch) {
         int* mem = reinterpret_cast<int*>(sbuf + ((max(k, 32) + 1) & ~1));  // 16-byte aligned
+        int* gather = top_k <= kGatherMax ? mem + (k * cap + 3) / 4 * 4 : nullptr;
         expand_row_prefetched(picks, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width,
-                              lengths + r, scan_smem, mem);
+                              lengths + r, scan_smem, mem, gather);
     } else {
         SmemPicks pk{picks};
         expand_row(pk, k, mr, Nr, cap, pos, window, sink, top_k, lists + (int64_t)r * width, width, lengths + r,
@@ -1107,6 +1111,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     dim3 grid((unsigned)chunks_x, (unsigned)R);
     int64_t k = top_p < N ? top_p : N;
     int64_t staged = k * cap <= kMemberPrefetch ? k * cap : 0;
+    if (staged && top_k <= kGatherMax) staged = (staged + 3) / 4 * 4 + top_k;  // + the gathered list
     int smem = sort_smem_bytes(most);
     if (smem < kFusedThreads * 8) smem = kFusedThreads * 8;
     if (smem < top_p * 8) smem = (int)(top_p * 8);
