@@ -198,3 +198,22 @@ def test_switch_rejects_unknown_impl(lsa, monkeypatch):
     monkeypatch.setenv("LSA_SELECT_IMPL", "bogus")
     with pytest.raises(ValueError, match="LSA_SELECT_IMPL"):
         lsa.flat_select(torch.zeros(2, 8, device=DEV), torch.tensor([7, 7], device=DEV), None, lsa.PortConfig())
+
+
+@pytest.mark.parametrize("P,cap,top_k", [(300, 6, 1024), (100, 12, 512), (4096, 16, 4096), (1024, 16, 16384)])
+def test_expand_staging_paths(oracle, lsa, P, cap, top_k):
+    """The expansion's three ways of reaching the member rows: staged with 16-byte copies
+    (cap % 4 == 0), staged with plain loads (cap % 4 != 0: 6), and the tiled walk from global
+    memory when the rows and the gathered list outgrow shared memory (4096 picks x 16; a
+    16384-id list) - all equal the checker's walk."""
+    rng = np.random.default_rng(P + cap)
+    rows = 3
+    member_rows = 5000
+    members = _members(member_rows, cap, P * 7 + cap, hi=60000)
+    picks = np.stack([rng.permutation(member_rows)[:P] for _ in range(rows)]).astype(np.int32)
+    picks[0, -5:] = -1  # short pick lists pad with -1
+    pos = np.array([60000, 30000, 511], np.int32)
+    want_l, want_n = oracle.expand(picks, members, pos, 64, 4, top_k)
+    tp, tm, tpos = (torch.from_numpy(x).to(DEV) for x in (picks, members, pos))
+    got_l, got_n = lsa.pipeline.expand_in_order(tp, tm, tpos, 64, 4, top_k)
+    assert (_np(got_l) == want_l).all() and (_np(got_n) == want_n).all()
