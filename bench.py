@@ -677,9 +677,9 @@ def run_batched(args, rank, world, dev):
         all_bytes, all_seqs = float(step_bytes), nb
     hbm, tflops, peak_kind = _load_peaks()
     value = all_bytes / (ms * 1e-3) / 1e9
-    # the dominant kernel: the read (persistent grid from one (row, KV head) unit per SM)
+    # the dominant kernel: the read (persistent grid from 16 (row, KV head) units up)
     read_bytes = n_ids * hkv_r * DH * 2 * 2 + nb * hkv_r * G * DH * 2 * 2 + n_ids * 4
-    persist = nb * hkv_r >= torch.cuda.get_device_properties(dev).multi_processor_count
+    persist = nb * hkv_r >= 16
     read_gbs = read_bytes / (us_read * 1e-6) / 1e9
     prof = _traffic_from_profile("sparse_read_persist_batched.md")
     traffic = None

@@ -940,13 +940,22 @@ static ReadPlan plan_read(int64_t R, int64_t Hkv, int64_t G, int64_t D, int64_t 
                           bool allow_persist = true) {
     ReadPlan p;
     int64_t units = R * Hkv;
-    if (splits_req <= 0 && allow_persist && units >= (int64_t)sms && width > 0 && (D == 64 || D == 128)) {
-        // bandwidth-bound batch: persistent grid (one CTA per SM), about four items per CTA
-        // (measured best: more items balance better but each adds a split merge), at least
-        // 512 ids per item; splits merge by ticket
+    if (splits_req <= 0 && allow_persist && units >= 16 && width > 0 && (D == 64 || D == 128)) {
+        // batches of at least 16 (row, KV head) units: the persistent grid (one CTA per SM)
+        // beat the split kernel at every size measured from 16 units up (two 2116-id decode
+        // rows: 12.7 vs 19.7 us; 64 x 4164-id rows: 264 vs 311 us); a single decode row (8
+        // units) stays on the split kernel (9.1 vs 12.4 us). Items per SM: about four when the
+        // units alone fill the SMs (more balance costs split merges), else enough splits for
+        // about one item per SM; at least 512 (resp. 256) ids per item. Splits merge by ticket.
         const int64_t slots = (int64_t)sms;
-        int64_t s = (4 * slots + units - 1) / units;
-        int64_t by_len = width / 512;
+        int64_t s, by_len;
+        if (units >= slots) {
+            s = (4 * slots + units - 1) / units;
+            by_len = width / 512;
+        } else {
+            s = (slots + units - 1) / units;
+            by_len = width / 256;
+        }
         if (s > by_len) s = by_len;
         if (s < 1) s = 1;
         const int64_t items = units * s;
