@@ -762,10 +762,8 @@ def run_tree1m(args, rank, world, dev):
     pos = torch.full((1,), C - 1, dtype=torch.int32, device=dev)
     scale = DH ** -0.5
 
-    qs, ks, vs = [q[b:b + 1] for b in range(B)], [k[b:b + 1] for b in range(B)], [v[b:b + 1] for b in range(B)]
-
-    def step():  # all sequences' candidates in one all-gather, all partials in a second
-        return seqshard.seqshard_decode_batch(qs, ks, vs, iq, pos, shards, pcfg, gather, scale)
+    def step():  # all sequences' candidates in one all-gather, one partial read, all partials in a second
+        return seqshard.seqshard_decode_batch(q, k, v, iq, pos, shards, pcfg, gather, scale)
 
     for _ in range(args.warmup):
         step()

@@ -194,28 +194,32 @@ def seqshard_decode(q, k_shard, v_shard, index_queries, positions, s: ShardIndex
     return merge_partials(outs.reshape(outs.shape[0], -1, D), lses.reshape(lses.shape[0], -1), q.dtype, q.shape)
 
 
-def seqshard_decode_batch(qs, ks, vs, index_queries, positions, shards, config, gather, scale=None):
+def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gather, scale=None):
     """One decode step of several sharded sequences with TWO exchanges in all: the candidate
     keys of every sequence in one all-gather, the partial outputs and log2-sum-exps of every
-    sequence in a second one, then one log-sum-exp merge over all of them.
+    sequence in a second one, then one log-sum-exp merge over all of them. The partial reads
+    of all sequences are ONE read call (the sequences as its batch rows).
 
-    qs[b] [1, R, Hq, D], this rank's ks[b] / vs[b] shard [1, length_b, Hkv, D], index_queries[b]
-    [R, d], shards[b] its ShardIndex; positions [R] shared. Returns [B, 1, R, Hq, D] in q's dtype,
-    equal to ``seqshard_decode`` sequence by sequence."""
+    q [B, R, Hq, D]; this rank's shard of every sequence k / v [B, length, Hkv, D] (every
+    sequence sharded alike: the shards start at the same position); index_queries[b] [R, d];
+    shards[b] the sequence's ShardIndex; positions [R] shared. Returns [B, R, Hq, D] in q's
+    dtype, matching ``seqshard_decode`` sequence by sequence."""
     B = len(shards)
+    if q.shape[0] != B or k.shape[0] != B or v.shape[0] != B:
+        raise ValueError("seqshard_decode_batch: one q / k / v batch row per shard index")
+    if any(s.start != shards[0].start for s in shards):
+        raise ValueError("seqshard_decode_batch: every sequence's shard must start at the same position")
     keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config) for b in range(B)])
     all_keys = gather(keys)  # [world, B, R, top_p]
     R = keys.shape[1]
-    outs, lses = [], []
+    lists, lengths = [], []
     for b in range(B):
         cand = all_keys[:, b].permute(1, 0, 2).reshape(R, -1)
-        lists, lengths = select_from_candidates(cand, positions, shards[b].members_global, config)
-        o, l = shard_partial_read(qs[b], ks[b], vs[b], lists[None], lengths[None], shards[b].start, scale)
-        outs.append(o)
-        lses.append(l)
-    D = outs[0].shape[-1]
-    packed = torch.cat([torch.stack(outs).reshape(-1, D), torch.stack(lses).reshape(-1, 1)], dim=1)  # [n, D + 1]
-    g = gather(packed)  # [world, n, D + 1]
-    q0 = qs[0]
-    merged = merge_partials(g[..., :D].contiguous(), g[..., D].contiguous(), q0.dtype, (B,) + tuple(q0.shape))
-    return merged
+        li, ln = select_from_candidates(cand, positions, shards[b].members_global, config)
+        lists.append(li)
+        lengths.append(ln)
+    out, lse = shard_partial_read(q, k, v, torch.stack(lists), torch.stack(lengths), shards[0].start, scale)
+    D = out.shape[-1]
+    packed = torch.cat([out.reshape(-1, D), lse.reshape(-1, 1)], dim=1)  # [B R Hq, D + 1]
+    g = gather(packed)  # [world, B R Hq, D + 1]
+    return merge_partials(g[..., :D].contiguous(), g[..., D].contiguous(), q.dtype, tuple(q.shape))

@@ -104,8 +104,8 @@ def test_partial_read_lse_and_empty_shard(lsa):
 
 def test_batched_step_equals_per_sequence(lsa, oracle):
     """The two-exchange step over several sequences (candidates of all sequences in one
-    gather, all partials in a second, one merge) equals the per-sequence step, here with one
-    rank (the gather adds the rank axis)."""
+    gather, one partial read for all of them, all partials in a second gather, one merge)
+    matches the per-sequence step, here with one rank (the gather adds the rank axis)."""
     from lsa_b200 import seqshard
 
     C = 16384
@@ -114,8 +114,9 @@ def test_batched_step_equals_per_sequence(lsa, oracle):
     gather = lambda x: x[None]
     pcfg = seqs[0][4]
     want = [seqshard.seqshard_decode(s[0], s[1], s[2], s[3], pos, s[6][0], pcfg, gather) for s in seqs]
-    got = seqshard.seqshard_decode_batch([s[0] for s in seqs], [s[1] for s in seqs], [s[2] for s in seqs],
-                                         [s[3] for s in seqs], pos, [s[6][0] for s in seqs], pcfg, gather)
-    assert got.shape == (3,) + tuple(seqs[0][0].shape)
-    for b in range(3):
-        assert torch.equal(got[b], want[b])
+    got = seqshard.seqshard_decode_batch(torch.cat([s[0] for s in seqs]), torch.cat([s[1] for s in seqs]),
+                                         torch.cat([s[2] for s in seqs]), [s[3] for s in seqs], pos,
+                                         [s[6][0] for s in seqs], pcfg, gather)
+    assert got.shape == (3,) + tuple(seqs[0][0].shape[1:])
+    for b in range(3):  # one batched read against three single-row reads: same lists, same keys
+        assert float((got[b].float() - want[b][0].float()).abs().max()) <= 2e-2
