@@ -126,10 +126,25 @@ def shard_candidates(index_queries, positions, s: ShardIndex, config) -> torch.T
 
 def select_from_candidates(all_keys, positions, members_global, config, top_k=None):
     """All ranks' candidates [R, ranks * top_p] -> the read lists every rank shares."""
-    top_k = config.top_k if top_k is None else int(top_k)
     best = pipeline.best_first_keys(all_keys.contiguous(), config.top_p)
-    picks = pipeline.unpack_ids(best)
-    return pipeline.expand_in_order(picks, members_global, positions, config.window_size, config.sink_size, top_k)
+    return expand_from_best(best, positions, members_global, config, top_k)
+
+
+def expand_from_best(best, positions, members_global, config, top_k=None):
+    """The expansion walk straight from the ordered packed keys [R, top_p] (no unpack pass)."""
+    top_k = config.top_k if top_k is None else int(top_k)
+    best = best.contiguous()
+    R, P = best.shape
+    width = top_k + config.window_size + config.sink_size
+    lists = torch.empty(R, width, dtype=torch.int32, device=best.device)
+    lengths = torch.empty(R, dtype=torch.int32, device=best.device)
+    if R:
+        mem = members_global.to(torch.int32).contiguous()
+        pos = positions.to(torch.int32).contiguous()
+        check(lib().lsa_expand_from_keys(ptr(best), R, P, P, ptr(mem), mem.shape[0], mem.shape[1], ptr(pos),
+                                         config.window_size, config.sink_size, top_k, ptr(lists), ptr(lengths),
+                                         stream_of(best)), "expand_from_best")
+    return lists, lengths
 
 
 def shard_partial_read(q, k_shard, v_shard, lists, lengths, start: int, scale=None):
@@ -212,10 +227,11 @@ def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gat
     keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config) for b in range(B)])
     all_keys = gather(keys)  # [world, B, R, top_p]
     R = keys.shape[1]
+    # the best top_p of every sequence's candidates in one launch, then each sequence's walk
+    best = pipeline.best_first_keys(all_keys.permute(1, 2, 0, 3).reshape(B * R, -1).contiguous(), config.top_p)
     lists, lengths = [], []
     for b in range(B):
-        cand = all_keys[:, b].permute(1, 0, 2).reshape(R, -1)
-        li, ln = select_from_candidates(cand, positions, shards[b].members_global, config)
+        li, ln = expand_from_best(best[b * R:(b + 1) * R], positions, shards[b].members_global, config)
         lists.append(li)
         lengths.append(ln)
     out, lse = shard_partial_read(q, k, v, torch.stack(lists), torch.stack(lengths), shards[0].start, scale)
