@@ -88,13 +88,14 @@ def _local_position(s: ShardIndex, pos: torch.Tensor) -> torch.Tensor:
     return local.clamp(min=0).to(torch.int32).contiguous()
 
 
-def shard_candidates(index_queries, positions, s: ShardIndex, config) -> torch.Tensor:
-    """The shard's best ``top_p`` packed keys [R, top_p] int64 with global bucket ids."""
+def shard_candidates(index_queries, positions, s: ShardIndex, config, local_positions=None) -> torch.Tensor:
+    """The shard's best ``top_p`` packed keys [R, top_p] int64 with global bucket ids.
+    ``local_positions``: the shard-local positions when already computed (shards alike)."""
     require_cuda(index_queries, positions, what="shard_candidates")
     if s.buckets.centroids_f32 is None:
         raise ValueError("the shard's tree scores buckets with centroids_f32")
     q = index_queries.float().contiguous()
-    pos = _local_position(s, positions)
+    pos = _local_position(s, positions) if local_positions is None else local_positions
     R, d = q.shape
     dev = q.device
     levels = s.hierarchy.levels
@@ -216,7 +217,8 @@ def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gat
     of all sequences are ONE read call (the sequences as its batch rows).
 
     q [B, R, Hq, D]; this rank's shard of every sequence k / v [B, length, Hkv, D] (every
-    sequence sharded alike: the shards start at the same position); index_queries[b] [R, d];
+    sequence sharded alike: the shards start at the same position and hold as many
+    positions); index_queries[b] [R, d];
     shards[b] the sequence's ShardIndex; positions [R] shared. Returns [B, R, Hq, D] in q's
     dtype, matching ``seqshard_decode`` sequence by sequence."""
     B = len(shards)
@@ -224,7 +226,10 @@ def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gat
         raise ValueError("seqshard_decode_batch: one q / k / v batch row per shard index")
     if any(s.start != shards[0].start for s in shards):
         raise ValueError("seqshard_decode_batch: every sequence's shard must start at the same position")
-    keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config) for b in range(B)])
+    if any(s.length != shards[0].length for s in shards):
+        raise ValueError("seqshard_decode_batch: every sequence's shard must hold the same positions")
+    local = _local_position(shards[0], positions)  # the same for every sequence
+    keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config, local) for b in range(B)])
     all_keys = gather(keys)  # [world, B, R, top_p]
     R = keys.shape[1]
     # the best top_p of every sequence's candidates in one launch, then each sequence's walk
