@@ -210,6 +210,31 @@ def seqshard_decode(q, k_shard, v_shard, index_queries, positions, s: ShardIndex
     return merge_partials(outs.reshape(outs.shape[0], -1, D), lses.reshape(lses.shape[0], -1), q.dtype, q.shape)
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _fan_out(fns, device):
+    """Run each callable on its own side stream forked from the current one (an event wait,
+    so it also forks a CUDA graph being captured), then join them back; the callables'
+    tensors are marked as used by the current stream. Each side stream keeps its own
+    workspaces (the package caches scratch and counters per stream)."""
+    main = torch.cuda.current_stream(device)
+    key = (device.index, len(fns))
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = [torch.cuda.Stream(device) for _ in fns]
+    out = []
+    for fn, st in zip(fns, _SIDE_STREAMS[key]):
+        st.wait_stream(main)
+        with torch.cuda.stream(st):
+            out.append(fn())
+    for st in _SIDE_STREAMS[key]:
+        main.wait_stream(st)
+    for r in out:
+        for t in (r if isinstance(r, tuple) else (r,)):
+            t.record_stream(main)
+    return out
+
+
 def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gather, scale=None):
     """One decode step of several sharded sequences with TWO exchanges in all: the candidate
     keys of every sequence in one all-gather, the partial outputs and log2-sum-exps of every
@@ -229,16 +254,17 @@ def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gat
     if any(s.length != shards[0].length for s in shards):
         raise ValueError("seqshard_decode_batch: every sequence's shard must hold the same positions")
     local = _local_position(shards[0], positions)  # the same for every sequence
-    keys = torch.stack([shard_candidates(index_queries[b], positions, shards[b], config, local) for b in range(B)])
+    dev = q.device
+    # the sequences' beams are independent chains of small launches: one side stream each
+    keys = torch.stack(_fan_out([lambda b=b: shard_candidates(index_queries[b], positions, shards[b], config, local)
+                                 for b in range(B)], dev))
     all_keys = gather(keys)  # [world, B, R, top_p]
     R = keys.shape[1]
     # the best top_p of every sequence's candidates in one launch, then each sequence's walk
     best = pipeline.best_first_keys(all_keys.permute(1, 2, 0, 3).reshape(B * R, -1).contiguous(), config.top_p)
-    lists, lengths = [], []
-    for b in range(B):
-        li, ln = expand_from_best(best[b * R:(b + 1) * R], positions, shards[b].members_global, config)
-        lists.append(li)
-        lengths.append(ln)
+    walks = _fan_out([lambda b=b: expand_from_best(best[b * R:(b + 1) * R], positions, shards[b].members_global,
+                                                    config) for b in range(B)], dev)
+    lists, lengths = [w[0] for w in walks], [w[1] for w in walks]
     out, lse = shard_partial_read(q, k, v, torch.stack(lists), torch.stack(lengths), shards[0].start, scale)
     D = out.shape[-1]
     packed = torch.cat([out.reshape(-1, D), lse.reshape(-1, 1)], dim=1)  # [B R Hq, D + 1]
