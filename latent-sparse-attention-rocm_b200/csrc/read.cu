@@ -599,6 +599,353 @@ __global__ void __launch_bounds__(kReadThreads) sparse_read_kernel(ReadArgs a) {
     merge_splits<T, D>(a, rh, row, h, red, tid);
 }
 
+// ------------------------------------------------------------------ decode read (latency path)
+
+// A handful of (row, KV head) units (single-sequence decode: 8 units of ~2k ids): one
+// cluster of up to 16 CTAs per unit, each CTA a contiguous slice of <= 256 list slots held
+// in shared memory at once, so the whole slice is ONE memory round trip after the ids:
+//   * after griddepcontrol.wait one load per thread brings the slice's ids, the row length
+//     and the query fragments (one round trip);
+//   * every K and V row of the slice is copied by 16-byte cp.async pieces (warp-wide, a
+//     slot's rows contiguous across lanes) in two commit groups (slots below 128, the
+//     rest), so the tensor-core stage of the first 128 slots runs while the tail lands;
+//   * the compute is the split kernel's mma_stage (S = q K^T and O += P V on mma.sync with
+//     the query heads as M); warps merge in shared memory with per-head weights computed
+//     once; output slice c belongs to cluster rank c, and every CTA stores its partial of
+//     each slice straight into the owner's shared-memory inbox (remote stores only: no
+//     remote load round trips), so one cluster barrier separates the pushes from the
+//     owners' merges.
+// No scratch, no counters, no spin: a call needs no workspace.
+constexpr int kDecodeReadSplits = 16;
+constexpr int kDecodeReadMaxSpan = kReadThreads;  // one id per thread
+
+template <typename T, int D, int GMAX>
+static constexpr int decode_red_bytes() {
+    // warp partials [NW][GMAX][D + 4] and (max, sum) [NW][GMAX][2], warp weights [NW][GMAX],
+    // the CTA's (max, sum) [GMAX][2], rank weights [16][GMAX], the slice's (max, sum) [GMAX][2]
+    return (kReadThreads / 32 * GMAX * (D + 4) + kReadThreads / 32 * GMAX * 3 + GMAX * 2 +
+            kDecodeReadSplits * GMAX + GMAX * 2) * 4;
+}
+
+// One warp's tensor-core pass over J n8 tiles of staged slots (8 J rows at kaddr / vaddr,
+// row stride D + 8 elements, listed flags fl), J in 1..4: S = q K^T with the query heads as M
+// (two accumulation chains per tile: even and odd k16 chunks), the online softmax update,
+// then O += P V in ceil(J / 2) k16 steps. Rows past the warp's J tiles are never addressed:
+// the upper half of an odd last k16 step re-reads the lower half (masked to zero).
+template <typename T, int D, int J>
+__device__ __forceinline__ void mma_pass(uint32_t kaddr, uint32_t vaddr, const unsigned char* fl,
+                                         const uint32_t (&qa)[D / 16][2], float (&o)[D / 8][4], float& mrow,
+                                         float& lrow, float scale_log2, int lane) {
+    constexpr int ROWS = D + 8, DC = D / 16, NT = D / 8, KT = (J + 1) / 2;
+    const int tq = lane & 3;
+    float sc[J][2];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        float s0[4] = {0.0f, 0.0f, 0.0f, 0.0f}, s1[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int q4 = 0; q4 < DC / 2; ++q4) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(kaddr + ((8 * j + (lane & 7)) * ROWS + (4 * q4 + (lane >> 3)) * 8) * 2, b0, b1, b2, b3);
+            mma16816<T>(s0, qa[2 * q4][0], 0u, qa[2 * q4][1], 0u, b0, b1);
+            mma16816<T>(s1, qa[2 * q4 + 1][0], 0u, qa[2 * q4 + 1][1], 0u, b2, b3);
+        }
+        sc[j][0] = s0[0] + s1[0];
+        sc[j][1] = s0[1] + s1[1];
+    }
+    float sv[2 * J];
+    float mx = kNegBig;
+#pragma unroll
+    for (int j = 0; j < J; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const float v = fl[8 * j + 2 * tq + e] ? sc[j][e] * scale_log2 : -INFINITY;
+            sv[2 * j + e] = v;
+            mx = fmaxf(mx, v);
+        }
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, 2));
+    const float mnew = fmaxf(mrow, mx);
+    const float alpha = exp2f(mrow - mnew);
+    mrow = mnew;
+    float pr[2 * J];
+    float psum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 2 * J; ++i) {
+        pr[i] = exp2f(sv[i] - mnew);
+        psum += pr[i];
+    }
+    lrow = lrow * alpha + psum;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        o[nt][0] *= alpha;
+        o[nt][1] *= alpha;
+    }
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt) {
+        const bool hi = 2 * kt + 1 < J;  // the step's upper 8 keys exist
+        const uint32_t pa0 = pack2<T>(pr[4 * kt], pr[4 * kt + 1]);
+        const uint32_t pa2 = hi ? pack2<T>(pr[(4 * kt + 2) % (2 * J)], pr[(4 * kt + 3) % (2 * J)]) : 0u;
+        // V rows of unlisted slots hold stale shared memory: zero their fragment halves so
+        // 0 * garbage cannot turn into NaN inside the MMA
+        const unsigned char* f = fl + 16 * kt;
+        const uint32_t vm0 = (f[2 * tq] ? 0x0000FFFFu : 0u) | (f[2 * tq + 1] ? 0xFFFF0000u : 0u);
+        const uint32_t vm1 = hi ? ((f[8 + 2 * tq] ? 0x0000FFFFu : 0u) | (f[9 + 2 * tq] ? 0xFFFF0000u : 0u)) : 0u;
+        const int key = 16 * kt + (lane & 7) + (hi ? 8 * ((lane >> 3) & 1) : 0);
+#pragma unroll
+        for (int np = 0; np < NT / 2; ++np) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(vaddr + (key * ROWS + (2 * np + (lane >> 4)) * 8) * 2, b0, b1, b2, b3);
+            mma16816<T>(o[2 * np], pa0, 0u, pa2, 0u, b0 & vm0, b1 & vm1);
+            mma16816<T>(o[2 * np + 1], pa0, 0u, pa2, 0u, b2 & vm0, b3 & vm1);
+        }
+    }
+}
+
+template <typename T, int D, int GMAX, int J>
+__global__ void __launch_bounds__(kReadThreads, 2) decode_read_kernel(ReadArgs a, int nslots) {
+    constexpr int SPW = 8 * J;  // slots per warp
+    static_assert(sizeof(T) == 2, "16-bit inputs");
+    constexpr int ROWS = D + 8;  // +16 B per row keeps ldmatrix conflict-free
+    constexpr int NW = kReadThreads / 32;
+    constexpr int LPR = D / 8;  // 16-byte pieces per row
+    extern __shared__ __align__(128) unsigned char smem[];
+    T* sK = reinterpret_cast<T*>(smem);                  // [nslots][ROWS]
+    T* sV = sK + (size_t)nslots * ROWS;                  // [nslots][ROWS]
+    __shared__ int sid[kDecodeReadMaxSpan];
+    __shared__ unsigned char sflag[kDecodeReadMaxSpan];
+    // partials pushed here by the cluster's CTAs: [splits][chunk] outputs + [splits][GMAX][2]
+    __shared__ float inbox[GMAX * D + kDecodeReadSplits * GMAX * 2 + kDecodeReadSplits];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int split = blockIdx.x, rh = blockIdx.y;
+    const int64_t row = rh / a.Hkv;
+    const int h = rh % a.Hkv;
+    const int64_t b = row / a.Tq;
+    const int G = a.G;
+    const int s0 = split * a.span;
+    // first cluster phase: every CTA of the cluster has started before any of them stores
+    // into a peer's inbox (waited on just before the pushes)
+    if (gridDim.x > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    pdl_wait();  // the list and lengths are the previous kernel's output
+    pdl_trigger();
+    int id = -1;
+    if (tid < a.span && s0 + tid < a.width) id = a.ids[row * a.width + s0 + tid] - a.id_base;
+    int len = a.lengths[row];
+    len = len < 0 ? 0 : (len > a.width ? a.width : len);
+    const int gq = lane >> 2, tq = lane & 3;
+    constexpr int DC = D / 16, NT = D / 8;
+    uint32_t qa[DC][2];
+#pragma unroll
+    for (int dc = 0; dc < DC; ++dc) {
+        const T* qp = reinterpret_cast<const T*>(a.q) + ((row * a.Hq) + h * G + gq) * D + dc * 16 + 2 * tq;
+        qa[dc][0] = gq < G ? *reinterpret_cast<const uint32_t*>(qp) : 0u;
+        qa[dc][1] = gq < G ? *reinterpret_cast<const uint32_t*>(qp + 8) : 0u;
+    }
+    const int n_here = max(0, min(s0 + a.span, len) - s0);
+    const bool ok = tid < n_here && id >= 0 && id < a.Tk;
+    sid[tid] = ok ? id : -1;
+    sflag[tid] = ok ? 1 : 0;
+    __syncthreads();
+    const T* kbase = reinterpret_cast<const T*>(a.k) + (b * a.Tk * a.Hkv + h) * D;
+    const T* vbase = reinterpret_cast<const T*>(a.v) + (b * a.Tk * a.Hkv + h) * D;
+    const int64_t tstride = (int64_t)a.Hkv * D;
+    auto issue = [&](int j0, int j1) {
+        for (int i = tid; i < (j1 - j0) * 2 * LPR; i += kReadThreads) {
+            const int j = j0 + i / (2 * LPR), pc = i % (2 * LPR);
+            const int idj = sid[j];
+            if (idj >= 0) {
+                const bool isv = pc >= LPR;
+                const int e = (pc % LPR) * 8;
+                const T* src = (isv ? vbase : kbase) + (int64_t)idj * tstride + e;
+                cp_async16(smem_u32((isv ? sV : sK) + (size_t)j * ROWS + e), src, 16);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue(0, n_here);
+
+    float o[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
+    float mrow = kNegBig, lrow = 0.0f;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    {
+        const int kb = warp * SPW;  // this warp's slots: one pass over the whole slice
+        if (kb < n_here) {
+            const unsigned char* fl = sflag + kb;
+            if (__any_sync(0xFFFFFFFFu, fl[lane % SPW] != 0))
+                mma_pass<T, D, J>(smem_u32(sK + (size_t)kb * ROWS), smem_u32(sV + (size_t)kb * ROWS), fl, qa, o,
+                                  mrow, lrow, a.scale_log2, lane);
+        }
+    }
+    __syncthreads();  // the K/V buffers become the reduction buffers
+    constexpr int RS = D + 4;                     // padded row: the fragment stores hit distinct banks
+    float* red = reinterpret_cast<float*>(smem);  // [NW][GMAX][RS]
+    float* redml = red + NW * GMAX * RS;          // [NW][GMAX][2]
+    float* wf = redml + NW * GMAX * 2;            // [NW][GMAX] weights of the warps' partials
+    float* cml = wf + NW * GMAX;                  // [GMAX][2] the CTA's (max, sum)
+    lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 1);
+    lrow += __shfl_xor_sync(0xFFFFFFFFu, lrow, 2);
+    if (gq < G) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+            *reinterpret_cast<float2*>(red + (warp * GMAX + gq) * RS + nt * 8 + 2 * tq) = make_float2(o[nt][0], o[nt][1]);
+        if (tq == 0) {
+            redml[(warp * GMAX + gq) * 2] = mrow;
+            redml[(warp * GMAX + gq) * 2 + 1] = lrow;
+        }
+    }
+    __syncthreads();
+    if (tid < NW * G) {  // (warp, query head): the head's max over the warps, this warp's weight
+        const int w = tid / G, g = tid % G;
+        float M = kNegBig;
+#pragma unroll
+        for (int w2 = 0; w2 < NW; ++w2) M = fmaxf(M, redml[(w2 * GMAX + g) * 2]);
+        wf[w * GMAX + g] = exp2f(redml[(w * GMAX + g) * 2] - M);
+        if (w == 0) cml[g * 2] = M;
+    }
+    __syncthreads();
+    if (tid < G) {
+        float L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) L += redml[(w * GMAX + tid) * 2 + 1] * wf[w * GMAX + tid];
+        cml[tid * 2 + 1] = L;
+    }
+    __syncthreads();
+    const int S = (int)gridDim.x;
+    if (S == 1) {
+        for (int oi = tid; oi < G * D; oi += kReadThreads) {
+            const int g = oi / D, e = oi % D;
+            float O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) O += red[(w * GMAX + g) * RS + e] * wf[w * GMAX + g];
+            write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, cml[g * 2], cml[g * 2 + 1]);
+        }
+        return;
+    }
+    // the cluster merge: output slice c (chunk outputs) belongs to rank c; every CTA stores
+    // its partial of each slice straight into the owner's inbox (remote stores, no remote
+    // loads), one cluster barrier, then each owner merges its slice from its own memory
+    cg::cluster_group cluster = cg::this_cluster();
+    const int total = G * D, chunk = (total + S - 1) / S;
+    float* in_o = inbox;                                // [S][chunk]
+    float* in_ml = inbox + S * chunk;                   // [S][GMAX][2] (S * chunk < G * D + 16)
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // (first phase)
+    for (int oi = tid; oi < total; oi += kReadThreads) {
+        const int g = oi / D, e = oi % D;
+        float O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) O += red[(w * GMAX + g) * RS + e] * wf[w * GMAX + g];
+        const int owner = oi / chunk;
+        cluster.map_shared_rank(in_o, owner)[split * chunk + (oi - owner * chunk)] = O;
+    }
+    if (tid < S * G) {
+        const int owner = tid / G, g = tid % G;
+        float* dst = cluster.map_shared_rank(in_ml, owner) + (split * GMAX + g) * 2;
+        dst[0] = cml[g * 2];
+        dst[1] = cml[g * 2 + 1];
+    }
+    cluster.sync();  // every partial is in its owner's inbox; nothing remote is touched after this
+    const int o0 = split * chunk;
+    // the heads this slice touches: [g0, g1]; per (rank, head) weight against the head's max
+    const int g0 = o0 / D, g1 = (min(o0 + chunk, total) - 1) / D;
+    float* rw = cml + GMAX * 2;                    // [S][GMAX]
+    float* rml = rw + kDecodeReadSplits * GMAX;    // [GMAX][2]
+    if (tid < S * G) {
+        const int r = tid / G, g = tid % G;
+        if (g >= g0 && g <= g1) {
+            float M = kNegBig;
+            for (int r2 = 0; r2 < S; ++r2) M = fmaxf(M, in_ml[(r2 * GMAX + g) * 2]);
+            rw[r * GMAX + g] = exp2f(in_ml[(r * GMAX + g) * 2] - M);
+            if (r == 0) rml[g * 2] = M;
+        }
+    }
+    __syncthreads();
+    if (tid < G && tid >= g0 && tid <= g1) {
+        float L = 0.0f;
+        for (int r = 0; r < S; ++r) L += in_ml[(r * GMAX + tid) * 2 + 1] * rw[r * GMAX + tid];
+        rml[tid * 2 + 1] = L;
+    }
+    __syncthreads();
+    for (int i = tid; i < chunk && o0 + i < total; i += kReadThreads) {
+        const int g = (o0 + i) / D, e = (o0 + i) % D;
+        float O = 0.0f;
+        for (int r = 0; r < S; ++r) O += in_o[r * chunk + i] * rw[r * GMAX + g];
+        write_out<T, D>(a, (row * a.Hq) + h * G + g, e, O, rml[g * 2], rml[g * 2 + 1]);
+    }
+}
+
+template <typename T, int D, int GMAX>
+static int decode_smem_bytes(int nslots) {
+    const int kv = 2 * nslots * (D + 8) * (int)sizeof(T);
+    const int red = decode_red_bytes<T, D, GMAX>();
+    return kv > red ? kv : red;
+}
+
+// Splits of the decode read for `units` (row, KV head) units of `width` slots, or 0 when
+// the call is not a decode-sized one (the split / persistent kernels take it).
+static int decode_read_splits(int64_t units, int64_t width, int sms) {
+    if (units <= 0 || width <= 0) return 0;
+    int s = (int)((width + kDecodeReadMaxSpan - 1) / kDecodeReadMaxSpan);  // at most 256 slots per CTA
+    if (s > kDecodeReadSplits) return 0;
+    int64_t want = (width + 127) / 128;  // at least ~128 slots per CTA are worth a CTA
+    if (want > kDecodeReadSplits) want = kDecodeReadSplits;
+    if (want > s) s = (int)want;
+    if (units * s > 2 * (int64_t)sms) return 0;  // more than one wave of two CTAs per SM
+    return s;
+}
+
+template <typename T, int D, int GMAX, int J>
+static int launch_decode_read_j(ReadArgs a, int64_t units, int splits, cudaStream_t st) {
+    const int nslots = (a.span + 8 * J - 1) / (8 * J) * (8 * J);  // whole warps of 8 J slots
+    const int smem = decode_smem_bytes<T, D, GMAX>(nslots);
+    auto kern = decode_read_kernel<T, D, GMAX, J>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+            cudaSuccess)
+        return LSA_ERR_CUDA;
+    if (splits > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        return LSA_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)splits, (unsigned)units);
+    cfg.blockDim = dim3(kReadThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    attrs[1].val.clusterDim.x = (unsigned)splits;
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, kern, a, nslots) != cudaSuccess) return LSA_ERR_CUDA;
+    return LSA_OK;
+}
+
+// slots per warp: 8 J with J the fewest n8 tiles that cover the slice in one pass
+template <typename T, int D, int GMAX>
+static int launch_decode_read(ReadArgs a, int64_t units, int splits, cudaStream_t st) {
+    a.splits = splits;
+    a.span = (a.width + splits - 1) / splits;
+    const int per_warp = (a.span + kReadThreads / 32 - 1) / (kReadThreads / 32);
+    if (per_warp <= 8) return launch_decode_read_j<T, D, GMAX, 1>(a, units, splits, st);
+    if (per_warp <= 16) return launch_decode_read_j<T, D, GMAX, 2>(a, units, splits, st);
+    if (per_warp <= 24) return launch_decode_read_j<T, D, GMAX, 3>(a, units, splits, st);
+    return launch_decode_read_j<T, D, GMAX, 4>(a, units, splits, st);
+}
+
+template <typename T, int D>
+static int dispatch_decode(const ReadArgs& a, int64_t units, int splits, cudaStream_t st) {
+    if (a.G <= 1) return launch_decode_read<T, D, 1>(a, units, splits, st);
+    if (a.G <= 2) return launch_decode_read<T, D, 2>(a, units, splits, st);
+    if (a.G <= 4) return launch_decode_read<T, D, 4>(a, units, splits, st);
+    if (a.G <= 8) return launch_decode_read<T, D, 8>(a, units, splits, st);
+    return LSA_ERR_ARG;
+}
+
 // ------------------------------------------------------------------ persistent read
 
 // Bandwidth-bound batches (at least one (row, KV head) unit per SM, 16-bit inputs): a
@@ -1111,6 +1458,17 @@ int sparse_read_launch(const void* q, const void* k, const void* v, int dtype, c
     a.out32 = out32;
     a.lse = lse;
     int64_t ctas = R * Hkv * p.splits;
+    // decode-sized calls (fewer than 16 units, splits not forced): the latency kernel
+    if (splits <= 0 && R * Hkv < 16 && (dtype == kBF16 || dtype == kF16)) {
+        const int ds = decode_read_splits(R * Hkv, width, num_sms());
+        if (ds > 0) {
+            if (dtype == kBF16)
+                return D == 64 ? dispatch_decode<__nv_bfloat16, 64>(a, R * Hkv, ds, stream)
+                               : dispatch_decode<__nv_bfloat16, 128>(a, R * Hkv, ds, stream);
+            return D == 64 ? dispatch_decode<__half, 64>(a, R * Hkv, ds, stream)
+                           : dispatch_decode<__half, 128>(a, R * Hkv, ds, stream);
+        }
+    }
     if (p.persist && (dtype == kBF16 || dtype == kF16)) {
         const int n_items = (int)ctas;
         if (dtype == kBF16)

@@ -696,6 +696,265 @@ __global__ void __launch_bounds__(kFusedThreads) select_cluster_kernel(
     }
 }
 
+// ------------------------------------------------------------------ decode select (latency path)
+
+// Rows of up to 16 x 16 x CPW visible buckets with top_p <= 32 (single-sequence decode):
+// one cluster of <= 16 CTAs per row, laid out so the chain after the previous kernel is as
+// short as it can be:
+//   * before griddepcontrol.wait every warp pulls its columns' centroid rows and member rows
+//     into L2 (prefetch only: the index is not produced by the kernel this one overlaps,
+//     but a hint cannot read stale data either way), so the scoring loads after the wait
+//     hit L2 instead of HBM;
+//   * after the wait, each warp issues the query and all its columns' centroid loads before
+//     the first FMA (canonical cdot: lane = chunk mod 32, fp32 fma chain in chunk order,
+//     butterfly), masks columns past the row's visible count to EMPTY, and each CTA sorts
+//     its own 16 CPW keys into one descending 32-list (warp bitonic sorts, in parallel
+//     across the cluster) that it stores into the leader's shared memory (DSMEM);
+//   * one cluster barrier (the other CTAs arrive and leave); the leader's warps merge the
+//     sorted lists pairwise (max(A[i], B[31 - i]) is bitonic and holds the top 32; a
+//     half-cleaner sorts it) in log2(cluster) levels;
+//   * the walk: warp w takes picks w and w + 16, loads their member rows straight into
+//     registers (32 slots per load, all loads in flight together), keeps ids in
+//     [sink, window_start) by ballots, counts per pick; pick offsets are warp reductions
+//     over the 32 counts; every kept id is stored at its offset (capped at top_k), then the
+//     window, the sinks and the -1 tail.
+// Identical output to select_cluster_kernel (same keys, same order, same walk).
+constexpr int kDecodeSelThreads = 512;
+constexpr int kDecodeSelWarps = kDecodeSelThreads / 32;
+constexpr int kDecodeMaxCap = 128;  // member slots per bucket the walk holds in registers
+
+template <typename TC>
+struct RawChunk;  // 8 consecutive elements of a centroid row, as loaded
+template <>
+struct RawChunk<__nv_bfloat16> {
+    uint4 v;
+    __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = __ldg(reinterpret_cast<const uint4*>(p)); }
+    __device__ __forceinline__ void get(float (&out)[8]) const {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f = __bfloat1622float2(h[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    }
+};
+template <>
+struct RawChunk<float> {
+    float4 a, b;
+    __device__ __forceinline__ void load(const float* p) {
+        a = __ldg(reinterpret_cast<const float4*>(p));
+        b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    }
+    __device__ __forceinline__ void get(float (&out)[8]) const {
+        out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+        out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    }
+};
+
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <typename TQ, typename TC, int CHUNKS, int CPW>
+__global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
+    const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d, RowPos rp, int64_t block,
+    int64_t bpb, int top_p, const int32_t* __restrict__ members, int cap, int window, int sink, int top_k,
+    int32_t* __restrict__ lists, int32_t* __restrict__ lengths) {
+    static_assert(CPW == 1 || CPW == 2 || CPW == 4, "16, 32 or 64 columns per CTA");
+    __shared__ int64_t lead[16 * 32];           // the cluster's sorted 32-lists (leader's copy is used)
+    __shared__ int64_t local[16 * CPW];         // this CTA's keys, column order
+    __shared__ int64_t half[32];                // CPW == 4: the second warp's sorted list
+    __shared__ int pick_bucket[32], pick_count[32];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+    const int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t Nr = rp.rows(r, N);
+    const int64_t c0 = (int64_t)rank * (kDecodeSelWarps * CPW);
+    const int nchunks = d >> 3;
+    const int mlines = (cap * 4 + 127) / 128;
+    // first cluster phase: every CTA has started before any of them writes the leader's
+    // shared memory (waited on just before that store)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    if (rp.table_off == nullptr) {
+        // the index is read-only here: pull this warp's centroid and member rows into L2
+        // while the previous kernel finishes
+        const int clines = (int)((int64_t)d * sizeof(TC) / 128);
+#pragma unroll
+        for (int i = 0; i < CPW; ++i) {
+            const int64_t n = c0 + warp + kDecodeSelWarps * i;
+            if (n < Nr) {
+                const char* base = reinterpret_cast<const char*>(c + n * d);
+                for (int l = lane; l < clines; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + l * 128));
+                if (lane < mlines) asm volatile("prefetch.global.L2 [%0];" ::"l"(members + n * cap + lane * 32));
+            }
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    const TC* cr = c + rp.off(r) * d;
+    const int32_t* mr = members + rp.off(r) * cap;
+    int64_t vis = rp.count_pos(r) / block * bpb;
+    const int64_t count = vis < 0 ? 0 : (vis < Nr ? vis : Nr);
+    // ---- scores: every load of the warp in flight before the first FMA
+    if (Nr > 0) {  // (block-uniform) loads are unconditional, at clamped valid addresses, so
+                   // the compiler issues all of them before the first use
+        float x[CHUNKS][8];
+        RawChunk<TC> raw[CPW][CHUNKS];
+#pragma unroll
+        for (int j = 0; j < CHUNKS; ++j) {
+            const int ch = min(lane + 32 * j, nchunks - 1);
+            load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+        }
+#pragma unroll
+        for (int i = 0; i < CPW; ++i) {
+            int64_t n = c0 + warp + kDecodeSelWarps * i;
+            n = n < Nr ? n : Nr - 1;  // a valid row; masked below
+#pragma unroll
+            for (int j = 0; j < CHUNKS; ++j) {
+                const int ch = min(lane + 32 * j, nchunks - 1);
+                raw[i][j].load(cr + n * d + (size_t)ch * 8);
+            }
+        }
+        float part[CPW];
+#pragma unroll
+        for (int i = 0; i < CPW; ++i) {
+            float p = 0.0f;
+#pragma unroll
+            for (int j = 0; j < CHUNKS; ++j) {
+                if (lane + 32 * j < nchunks) {
+                    float y[8];
+                    raw[i][j].get(y);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) p = __fmaf_rn(x[j][e], y[e], p);
+                }
+            }
+            part[i] = p;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+            for (int i = 0; i < CPW; ++i) part[i] = __fadd_rn(part[i], __shfl_xor_sync(0xFFFFFFFFu, part[i], off));
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int i = 0; i < CPW; ++i) {
+                const int64_t n = c0 + warp + kDecodeSelWarps * i;
+                local[warp + kDecodeSelWarps * i] = n < count ? pack_key(part[i], (int32_t)n) : kEmpty;
+            }
+        }
+    } else if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < CPW; ++i) local[warp + kDecodeSelWarps * i] = kEmpty;
+    }
+    __syncthreads();
+    // ---- this CTA's keys as one sorted 32-list in the leader's shared memory
+    int64_t* lead0 = cluster.map_shared_rank(lead, 0);
+    if (CPW == 4 && warp == 1) half[lane] = warp_sort32_desc(local[32 + lane], lane);
+    if (CPW == 4) __syncthreads();
+    cluster_wait_acquire();  // (first phase)
+    if (warp == 0) {
+        int64_t x = (CPW == 1 && lane >= 16) ? kEmpty : local[lane];
+        x = warp_sort32_desc(x, lane);
+        if (CPW == 4) {
+            const int64_t y = half[31 - lane];
+            x = warp_clean32_desc(x > y ? x : y, lane);
+        }
+        lead0[rank * 32 + lane] = x;
+    }
+    cluster_arrive_release();
+    if (rank != 0) return;  // the leader alone reads the keys; nothing reads this CTA's memory
+    cluster_wait_acquire();
+    // ---- merge tree over the cs sorted lists (warp w holds list w)
+    int64_t x = warp < cs ? lead[warp * 32 + lane] : kEmpty;
+    for (int step = 1; step < cs; step <<= 1) {
+        if ((warp % (2 * step)) == 0 && warp + step < cs) {
+            const int64_t y = lead[(warp + step) * 32 + 31 - lane];
+            x = warp_clean32_desc(x > y ? x : y, lane);
+            lead[warp * 32 + lane] = x;
+        }
+        __syncthreads();
+    }
+    const int k = (int)min((int64_t)top_p, Nr);
+    if (warp == 0) pick_bucket[lane] = lane < k ? key_bucket(x) : -1;
+    __syncthreads();
+    // ---- the walk over the picks' member rows
+    const int64_t pos = rp.walk_pos(r);
+    int64_t ws = pos + 1 - window;
+    if (ws < 0) ws = 0;
+    const int nch = (cap + 31) >> 5;
+    constexpr int kMaxCh = kDecodeMaxCap / 32;
+    int vals[2][kMaxCh];
+    if (Nr > 0) {  // (block-uniform) unconditional loads at clamped valid addresses
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int b = pick_bucket[warp + kDecodeSelWarps * t];
+            const int64_t row = b >= 0 ? b : 0;
+#pragma unroll
+            for (int ch = 0; ch < kMaxCh; ++ch) vals[t][ch] = __ldcg(mr + row * cap + min(ch * 32 + lane, cap - 1));
+        }
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int b = pick_bucket[warp + kDecodeSelWarps * t];
+#pragma unroll
+            for (int ch = 0; ch < kMaxCh; ++ch)
+                if (b < 0 || ch >= nch || ch * 32 + lane >= cap) vals[t][ch] = -1;
+        }
+    } else {
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int ch = 0; ch < kMaxCh; ++ch) vals[t][ch] = -1;
+    }
+    unsigned masks[2][kMaxCh];
+    int cnt[2] = {0, 0};
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+#pragma unroll
+        for (int ch = 0; ch < kMaxCh; ++ch) {
+            const int v = vals[t][ch];
+            const bool keep = v >= 0 && v >= sink && (int64_t)v < ws;
+            masks[t][ch] = __ballot_sync(0xFFFFFFFFu, keep);
+            cnt[t] += __popc(masks[t][ch]);
+        }
+    }
+    if (lane == 0) {
+        pick_count[warp] = cnt[0];
+        pick_count[warp + kDecodeSelWarps] = cnt[1];
+    }
+    __syncthreads();
+    const int mine = pick_count[lane];
+    const int total = __reduce_add_sync(0xFFFFFFFFu, (unsigned)mine);
+    const int filled = total < top_k ? total : top_k;
+    const int width = top_k + window + sink;
+    int32_t* out = lists + (int64_t)r * width;
+    const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+        const int p = warp + kDecodeSelWarps * t;
+        int at = (int)__reduce_add_sync(0xFFFFFFFFu, lane < p ? (unsigned)mine : 0u);
+#pragma unroll
+        for (int ch = 0; ch < kMaxCh; ++ch) {
+            const int o = at + __popc(masks[t][ch] & lt);
+            if (((masks[t][ch] >> lane) & 1u) && o < top_k) out[o] = vals[t][ch];
+            at += __popc(masks[t][ch]);
+        }
+    }
+    int nwin = (int)(pos - ws + 1);
+    if (nwin < 0) nwin = 0;
+    const int nsink = (int)(sink < ws ? sink : ws);
+    for (int i = threadIdx.x; i < width - filled; i += kDecodeSelThreads) {
+        int v = -1;
+        if (i < nwin) v = (int)(ws + i);
+        else if (i < nwin + nsink) v = i - nwin;
+        out[filled + i] = v;
+    }
+    if (threadIdx.x == 0) lengths[r] = filled + nwin + nsink;
+}
+
 // ------------------------------------------------------------------ host helpers
 
 // ------------------------------------------------------------------ streaming select
@@ -1216,6 +1475,56 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     cudaLaunchAttribute cattrs[2];
     cattrs[0] = pdl;
     cattrs[1].id = cudaLaunchAttributeClusterDimension;
+    // single-sequence decode rows (top_p <= 32): the latency path, one cluster per row
+    const int dcpw = cpw <= 1 ? 1 : (cpw <= 2 ? 2 : 4);
+    // (registers: the warp holds its columns' raw chunks, at most 8 x 16 bytes per lane)
+    if (use_cluster && top_p <= 32 && cap <= kDecodeMaxCap && (d % 8) == 0 &&
+        (c_dtype == kBF16 || c_dtype == kF32) && ch * dcpw * (c_dtype == kF32 ? 2 : 1) <= 8) {
+        const int dcs = (int)((most + kDecodeSelWarps * dcpw - 1) / (kDecodeSelWarps * dcpw));
+        cattrs[1].val.clusterDim.x = (unsigned)(dcs < 1 ? 1 : dcs);
+        cattrs[1].val.clusterDim.y = 1;
+        cattrs[1].val.clusterDim.z = 1;
+        cudaLaunchConfig_t dc = {};
+        dc.gridDim = dim3(cattrs[1].val.clusterDim.x, (unsigned)R);
+        dc.blockDim = dim3(kDecodeSelThreads);
+        dc.dynamicSmemBytes = 0;
+        dc.stream = stream;
+        dc.attrs = cattrs;
+        dc.numAttrs = 2;
+        int rc = LSA_ERR_ARG;
+#define LSA_DS(TQ, TC, CH)                                                                                       \
+    do {                                                                                                         \
+        auto launch = [&](auto kern) -> int {                                                                    \
+            if (dcs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=      \
+                               cudaSuccess)                                                                      \
+                return LSA_ERR_CUDA;                                                                             \
+            return cudaLaunchKernelEx(&dc, kern, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d,       \
+                                      positions, block, bpb, (int)top_p, members, (int)cap, (int)window,         \
+                                      (int)sink, (int)top_k, lists, lengths) == cudaSuccess                      \
+                       ? LSA_OK                                                                                  \
+                       : LSA_ERR_CUDA;                                                                           \
+        };                                                                                                       \
+        if (dcpw == 1) rc = launch(select_decode_kernel<TQ, TC, CH, 1>);                                         \
+        else if (dcpw == 2) rc = launch(select_decode_kernel<TQ, TC, CH, 2>);                                    \
+        else rc = launch(select_decode_kernel<TQ, TC, CH, 4>);                                                   \
+    } while (0)
+#define LSA_DS_CH(TQ, TC)                  \
+    do {                                   \
+        if (ch <= 1) LSA_DS(TQ, TC, 1);      \
+        else if (ch <= 2) LSA_DS(TQ, TC, 2); \
+        else if (ch <= 4) LSA_DS(TQ, TC, 4); \
+        else LSA_DS(TQ, TC, 8);              \
+    } while (0)
+        if (q_dtype == kBF16 && c_dtype == kBF16) LSA_DS_CH(__nv_bfloat16, __nv_bfloat16);
+        else if (q_dtype == kF32 && c_dtype == kF32) LSA_DS_CH(float, float);
+        else if (q_dtype == kF32 && c_dtype == kBF16) LSA_DS_CH(float, __nv_bfloat16);
+        else return LSA_ERR_ARG;
+#undef LSA_DS_CH
+#undef LSA_DS
+        if (rc != LSA_OK) return rc;
+        LSA_LAUNCH_CHECK();
+        return LSA_OK;
+    }
     cattrs[1].val.clusterDim.x = (unsigned)cs;
     cattrs[1].val.clusterDim.y = 1;
     cattrs[1].val.clusterDim.z = 1;

@@ -58,6 +58,37 @@ def test_decode_row_splits_vs_oracle(oracle, lsa, splits):
     _check(_read(tq, tk, tv, ids, ln, 128 ** -0.5, splits=splits), want, torch.float32)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("width", [40, 200, 2116, 3000, 4000])
+@pytest.mark.parametrize("hq,hkv,D", [(32, 8, 128), (8, 1, 64), (2, 2, 128), (16, 2, 64)])
+def test_decode_read_shapes_vs_oracle(oracle, lsa, dtype, width, hq, hkv, D):
+    """The decode-sized read (fewer than 16 (row, KV head) units, one cluster per unit):
+    one CTA (40 ids) up to 16 CTAs of 8-32 slots per warp (4000 ids); out-of-range ids, -1
+    pads and a length below the width are skipped."""
+    rng = np.random.default_rng(width + hq + D)
+    Tk = 4096
+    ids = rng.integers(-1, Tk + 5, (1, 1, width)).astype(np.int32)
+    lengths = np.array([[width - 3]], np.int32)
+    tq, tk, tv, i, ln, want = _case(oracle, 1, 1, Tk, hq, hkv, D, width, dtype, width, lengths=lengths, ids=ids)
+    _check(lsa.read_kernel_tiled.sparse_read_auto(tq, tk, tv, i, ln, D ** -0.5), want, dtype)
+
+
+def test_decode_partial_read_vs_oracle(oracle, lsa):
+    """The sequence-shard partial read of a decode row: fp32 output and log2-sum-exp over
+    this shard's keys (global ids offset by the shard start) match the oracle's read."""
+    from lsa_b200 import seqshard
+
+    rng = np.random.default_rng(5)
+    Tk, start, width = 2048, 1024, 2116
+    ids = (rng.integers(0, Tk, (1, 1, width)) + start).astype(np.int32)
+    tq, tk, tv, i, ln, _ = _case(oracle, 1, 1, Tk, 32, 8, 128, width, torch.bfloat16, 6, ids=ids - start)
+    out, lse = seqshard.shard_partial_read(tq, tk, tv, torch.from_numpy(ids).to(DEV), ln, start, 128 ** -0.5)
+    want = oracle.sparse_read(tq.float().cpu().numpy(), tk.float().cpu().numpy(), tv.float().cpu().numpy(),
+                              ids - start, ln.cpu().numpy())
+    assert float(np.abs(out.view(1, 1, 32, 128).cpu().numpy() - want).max()) <= TOL[torch.bfloat16]
+    assert torch.isfinite(lse).all()
+
+
 def test_batch_ragged_pad_boundary(oracle, lsa):
     rng = np.random.default_rng(3)
     B, T, width = 3, 13, 128
