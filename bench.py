@@ -2,30 +2,43 @@
 
 Workload ("decode32k"): B=1, one query token, Hq=32, Hkv=8, Dh=128, bf16, drift keys,
 64-token buckets in 512-token cluster blocks (8 per block, cap 128, pools of 4), top-32
-buckets (2048-token budget), window 64, sinks 4 - the D-LSA Flat arm through the fused
-select (LSA_SELECT_IMPL=fused: one launch from index query to read lists) and the split-K
-TMA-gather read. A STEP is one decoded token through LAYERS = 32 layers, each layer its
-own independent 32k KV cache (4.3 GB of K/V in all), so one step touches 32 x ~9.7 MB,
-more than twice the 126 MB L2, before any cache is revisited: no L2 flush is needed.
-The select+read index (buckets) is built before timing, as in the reference's bench
-(src/lsa_rocm_lab/port/bench.py:113-154 times select+read on a prebuilt index).
+buckets (2048-token budget), window 64, sinks 4 - the D-LSA Flat arm: the one-launch select
+(LSA_SELECT_IMPL=fused) and the sparse read. A STEP is one decoded token through LAYERS = 32
+layers, each layer its own independent 32k KV cache (4.3 GB of K/V in all), so one step
+touches 32 x ~9.7 MB, more than twice the 126 MB L2, before any cache is revisited: no L2
+flush is needed. The select+read index (buckets) is built before timing, as in the
+reference's bench (src/lsa_rocm_lab/port/bench.py:113-154 times select+read on a prebuilt
+index).
+
+Before any number is printed, layer 0's read lists are checked bit-exactly and its output
+within 2e-2 against the CPU checker (oracle/); a mismatch exits non-zero without a line (the
+reference refuses to benchmark when its gates fail, src/lsa_rocm_lab/kernel_adapter.py:177-186).
 
 value = algorithmic bytes of the step / step time, in GB/s (whole job: summed over the
-N replica ranks, max time over ranks); us_per_select_read = step time / LAYERS. The
-device-timed region replays one CUDA graph of the K steps' kernels with inputs resident.
-``e2e`` is the same metric through the public Python API with host buffers: every step
-copies the 32 layers' query rows from pinned host memory, runs make_index_space +
-flat_select + lsa_read per layer, and copies the outputs back - the step captured once in a
-CUDA graph whose replays include both copies (``eager_*`` keys: the same step launched
-eagerly from Python, host-bound).
+N ranks, max time over ranks); us_per_select_read = step time / LAYERS. The device-timed
+region replays a CUDA graph of one step K times with inputs resident, an event after every
+replay: ``timing`` holds p50 / p95 / min / max / MAD over those K steps
+(src/lsa_rocm_lab/port/bench.py:51-64). ``e2e`` is the same metric through the public
+Python API with host buffers: every step copies the 32 layers' query rows from pinned host
+memory, runs make_index_space + flat_select + lsa_read per layer, and copies the outputs
+back - the step captured once in a CUDA graph whose replays include both copies
+(``eager_*`` keys: the same step launched eagerly from Python, host-bound).
+
+The other configurations ride in the same line: ``prefill`` (configs[2], one GPU),
+``sharded`` (configs[3] batched 128k decode sharded by KV head, configs[4] tree decode of
+1M-token sequences sharded by sequence - on every GPU count, so the N-GPU runs carry their
+scaling) and ``cpu_baselines`` (the CPU checker on this box's host cores for configs 1-5,
+bounded samples).
 
 ``--impl reference`` times the reference's CPU path for this workload on the host cores:
 the CPU checker (oracle/, a restatement of the reference's select + read; the reference's
-own path needs the absent upstream package and a ROCm GPU) over a bounded sample of
-select+reads per step, with one worker process per core.
+own path needs the absent upstream package and a ROCm GPU) builds the index and runs a
+bounded sample of select+reads per step, one worker process per core; it loads no CUDA
+library of this repository.
 
-Multi-GPU (--gpus N under torchrun): the decode of one sequence does not shard, so the N
-ranks run independent replicas (scaling "weak"); no collective is on the data path.
+Multi-GPU (--gpus N under torchrun): the decode of one sequence does not shard, so the
+headline runs N independent replicas (scaling "weak"; no collective on its data path);
+``sharded`` runs the two configurations that do shard, with their NCCL exchanges.
 """
 
 from __future__ import annotations
@@ -131,7 +144,67 @@ def _traffic_from_profile(name: str):
     return _profile_field(name, "traffic_bytes_per_launch")
 
 
+def _dist(ms: list) -> dict:
+    """p50 / p95 / min / max / MAD of per-step times (ms), as the reference's summarize
+    (src/lsa_rocm_lab/port/bench.py:51-64)."""
+    xs = sorted(ms)
+    n = len(xs)
+    if not n:
+        return {}
+    p50 = statistics.median(xs)
+    p95 = xs[min(n - 1, int(math.ceil(0.95 * n)) - 1)]
+    mad = statistics.median([abs(x - p50) for x in xs])
+    return {"samples": n, "p50_ms": round(p50, 5), "p95_ms": round(p95, 5), "min_ms": round(xs[0], 5),
+            "max_ms": round(xs[-1], 5), "mad_ms": round(mad, 5)}
+
+
+def _lscpu_model() -> str:
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return "unknown"
+
+
+class GateError(RuntimeError):
+    """The timed path disagrees with the CPU checker: no number may be reported."""
+
+
+def gate_decode(L, lists, lengths, out) -> dict:
+    """Layer 0 of the decode step against the CPU checker on the same index: the read lists
+    bit-exact, the output within 2e-2 (bf16)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    b = L["buckets"]
+    ob = O.Buckets(b.centroids_f32.cpu().numpy(), b.centroids.float().cpu().numpy(), b.members.cpu().numpy(),
+                   b.sizes.cpu().numpy(), b.key_sums.cpu().numpy())
+    want_l, want_n = O.flat_select(L["iq"].float().cpu().numpy(), np.array([T_CTX - 1]), ob, O.Config(**CFG))
+    got_l, got_n = lists.cpu().numpy(), lengths.cpu().numpy()
+    if not (np.array_equal(got_l, want_l) and np.array_equal(got_n, want_n)):
+        raise GateError("decode32k layer 0: read lists differ from the CPU checker")
+    want_o = O.sparse_read(L["q"].float().cpu().numpy(), L["k"].float().cpu().numpy(), L["v"].float().cpu().numpy(),
+                           want_l[None], want_n[None], DH ** -0.5)
+    err = float(np.abs(out.float().cpu().numpy() - want_o).max())
+    if not err <= 2e-2:
+        raise GateError(f"decode32k layer 0: output max abs err {err} > 2e-2")
+    return {"lists_bit_exact": True, "output_max_abs_err": err, "tolerance": 2e-2, "checker": "oracle/ (CPU)"}
+
+
 # --------------------------------------------------------------------------- B200 arm
+
+
+def decode_config(world, decode_impl="split"):
+    """The decode32k line's config (the same dict on the B200 and the reference arms)."""
+    return {"workload": "decode32k", "layers_per_step": LAYERS, "context": T_CTX, "batch": 1, "heads_q": HQ,
+            "heads_kv": HKV, "head_dim": DH, "bucket_size": CFG["bucket_size"], "top_p_buckets": CFG["top_p"],
+            "budget_tokens": CFG["top_k"], "window": CFG["window_size"], "sink": CFG["sink_size"],
+            "decode_impl": decode_impl, "parallelism": f"replicas{world}",
+            "l2": "no flush: 32 independent 32k caches, each step touches 32 x ~9.7 MB > 2x L2"}
 
 
 def build_layers(dev, lsa, arms=False):
@@ -200,7 +273,9 @@ def run_b200(args, rank, world, dev):
         for _ in range(max(args.warmup, 3)):
             step()
         sel = [select(L) for L in layers]
+        out0 = read(layers[0], *sel[0])
         stream.synchronize()
+    gate = gate_decode(layers[0], sel[0][0], sel[0][1], out0)  # raises GateError on a mismatch
     lengths_all = [int(s[1].item()) for s in sel]
     n_ids = sum(lengths_all)
     members_bytes = LAYERS * CFG["top_p"] * CFG["bucket_cap"] * 4
@@ -212,11 +287,10 @@ def run_b200(args, rank, world, dev):
     step_bytes = centroid_bytes + members_bytes + kv_bytes + small
     read_bytes_per_launch = (kv_bytes + n_ids * 4) / LAYERS + HQ * DH * 2 * 2
 
-    # one graph holding K steps (LAYERS select+read pairs each)
+    # one graph holding one step (LAYERS select+read pairs), replayed K times
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for _ in range(args.steps):
-            step()
+        step()
     split_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(split_graph, stream=stream):
         for _ in range(args.steps):
@@ -260,8 +334,30 @@ def run_b200(args, rank, world, dev):
             torch.distributed.barrier()
         return ev0.elapsed_time(ev1) / reps
 
+    def timed_steps(g, steps):
+        """K replays of a one-step graph between a barrier and synchronisations; an event
+        after every replay gives the per-step distribution."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                g.replay()
+            stream.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            torch.cuda.synchronize(dev)
+            evs[0].record(stream)
+            for i in range(steps):
+                g.replay()
+                evs[i + 1].record(stream)
+            stream.synchronize()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        per = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+        return evs[0].elapsed_time(evs[-1]), per
+
     with ClockSampler(dev.index) as clocks:
-        ms_total = timed(graph)
+        ms_total, per_step = timed_steps(graph, args.steps)
     ms_read = timed(read_graph)
     ms_select = timed(select_graph)
     ms_split = timed(split_graph)
@@ -437,11 +533,9 @@ def run_b200(args, rank, world, dev):
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded drift keys, N(0,1) q/v)",
-        "config": {"workload": "decode32k", "layers_per_step": LAYERS, "context": T_CTX, "batch": 1,
-                   "heads_q": HQ, "heads_kv": HKV, "head_dim": DH, "bucket_size": CFG["bucket_size"],
-                   "top_p_buckets": CFG["top_p"], "budget_tokens": CFG["top_k"], "window": CFG["window_size"],
-                   "sink": CFG["sink_size"], "decode_impl": args.decode_impl, "parallelism": f"replicas{world}",
-                   "l2": "no flush: 32 independent 32k caches, each step touches 32 x ~9.7 MB > 2x L2"},
+        "config": decode_config(world, args.decode_impl),
+        "timing": {**_dist(per_step), "note": "per step (LAYERS select+read pairs), this rank"},
+        "gate": gate,
         "us_per_select_read": round(ms_per_step / LAYERS * 1e3, 3),
         "us_per_select_read_split": round(ms_split / args.steps / LAYERS * 1e3, 3),
         "us_per_select_read_fused": round(ms_fused / args.steps / LAYERS * 1e3, 3),
@@ -476,7 +570,7 @@ def run_b200(args, rank, world, dev):
 # --------------------------------------------------------------------------- prefill leg
 
 
-def run_prefill(args, dev):
+def run_prefill(args, dev, dump=None):
     """cfg 3: prefill select+read at T tokens (default 32k), bf16, per-64-query-tile top-32.
 
     Times, on inputs resident in HBM (q 268 MB + K/V 134 MB at 32k, larger than L2, so
@@ -534,6 +628,15 @@ def run_prefill(args, dev):
                                                                         enable_gqa=True)
 
         ms_dense = timed(dense, max(2, reps // 2))
+    if dump is not None and T >= 64 * 401:  # the CPU baseline's sample: a tile in the last quarter
+        import numpy as np
+
+        t = 400
+        path = os.path.join(dump["dir"], "prefill.npz")
+        np.savez(path, **_np_buckets(buckets), iq=iq.float().cpu().numpy(),
+                 q=q[:, t * 64:(t + 1) * 64].float().cpu().numpy(), k=k.float().cpu().numpy(),
+                 v=v.float().cpu().numpy(), tile=np.int64(t))
+        dump["prefill"] = path
     hbm, tflops, peak_kind = _load_peaks()
     achieved = flops / (ms_read * 1e-3) / 1e12
     return {
@@ -561,33 +664,39 @@ BATCH_CFG = dict(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap
                  window_size=64, sink_size=4)
 
 
-def run_batched(args, rank, world, dev):
+def run_batched(args, rank, world, dev, mode=None, dump=None):
     """cfg 4: B = 64 sequences, lengths ~ U[65536, 131072] (seeded), Hq 64 / Hkv 8 / Dh 128,
     bf16, q/k/v ~ N(0, 1), top-64 buckets (4096-token budget), window 64, sinks 4.
-    Sharding (no collective either way; total work fixed -> "strong"):
-      heads (default, the configuration's own): every rank holds all 64 sequences' index
-        (centroids and members, replicated) and selects for all of them - the selection is
-        shared by the heads - then reads only its Hkv / N KV heads (and their q heads);
-      sequences: rank r owns sequences shard_rows(64, world, r) with all their heads.
-    A step = one token for every sequence: one batched-select launch + one read launch,
+    Sharding (total work fixed -> "strong"):
+      heads (default, the configuration's own): rank r holds KV heads [r Hkv/N, (r+1) Hkv/N)
+        of all 64 sequences and the index of its share of the sequences; it selects that
+        share, one NCCL all-gather gives every rank every sequence's read list, and it reads
+        its heads of all sequences (batched.head_sharded_select);
+      heads_replicated: as heads, but every rank holds the whole index and selects for all
+        64 sequences (no collective; the selection is repeated on every rank);
+      sequences: rank r owns sequences shard_rows(64, N, r) with all their heads.
+    A step = one token for every sequence: select (+ the gather) + one read launch,
     replayed from a CUDA graph. One step reads ~1.1 GB of K/V at N = 1 (> L2): no flush."""
     import torch
 
     import lsa_b200 as lsa
-    from lsa_b200 import batched
+    from lsa_b200 import batched, seqshard
     from lsa_b200.index_space import index_keys, index_queries
 
+    mode = mode or args.batched_shard
     B, HQB = args.batched_seqs, 64
     len_lo, len_hi = (int(x) for x in args.batched_len.split(","))
-    by_heads = args.batched_shard == "heads"
-    if by_heads and HKV % world:
+    if mode != "sequences" and HKV % world:
         raise ValueError(f"head sharding needs {HKV} KV heads to divide over {world} ranks")
+    if mode == "heads" and B % world:
+        mode = "heads_replicated"  # equal selection shares are needed for the all-gather
     gen = torch.Generator(device="cpu")
     gen.manual_seed(SEED + 4)
     lengths_all = torch.randint(len_lo, len_hi + 1, (B,), generator=gen).tolist()
-    start, end = (0, B) if by_heads else batched.shard_rows(B, world, rank)
-    lengths = lengths_all[start:end]
-    h0, h1 = (rank * HKV // world, (rank + 1) * HKV // world) if by_heads else (0, HKV)
+    seq0, seq1 = (0, B) if mode != "sequences" else batched.shard_rows(B, world, rank)  # K/V held
+    sel0, sel1 = batched.shard_rows(B, world, rank) if mode != "heads_replicated" else (0, B)  # selected
+    h0, h1 = (rank * HKV // world, (rank + 1) * HKV // world) if mode != "sequences" else (0, HKV)
+    lengths = lengths_all[seq0:seq1]
     G = HQB // HKV
     pcfg = lsa.PortConfig(**BATCH_CFG)
     Tmax = max(lengths) if lengths else 1
@@ -597,84 +706,126 @@ def run_batched(args, rank, world, dev):
     v = torch.empty(nb, Tmax, h1 - h0, DH, dtype=torch.bfloat16, device=dev)
     iqs, per_seq = [], []
     for i, L in enumerate(lengths):  # per sequence (seeded by the sequence, not the rank)
+        sid = seq0 + i
         g = torch.Generator(device=dev)
-        g.manual_seed(SEED + 4 + 1000 * (start + i))
+        g.manual_seed(SEED + 4 + 1000 * sid)
         qf = torch.randn(1, HQB, DH, generator=g, device=dev).to(torch.bfloat16)
         kf = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
         q[i] = qf[:, h0 * G:h1 * G]
         k[i] = kf[:, h0:h1]
         v[i] = torch.randn(Tmax, HKV, DH, generator=g, device=dev).to(torch.bfloat16)[:, h0:h1]
-        iqs.append(index_queries(qf, HKV))
-        per_seq.append(lsa.build_buckets_gpu(index_keys(kf[:L]), pcfg))
+        if sel0 <= sid < sel1:
+            iqs.append(index_queries(qf, HKV))
+            per_seq.append(lsa.build_buckets_gpu(index_keys(kf[:L]), pcfg))
         del kf
     iq = torch.cat(iqs)
     bb = batched.concat_buckets(per_seq)
+    pos = torch.tensor([L - 1 for L in lengths_all[sel0:sel1]], dtype=torch.int32, device=dev)
+    if dump is not None and world == 1:  # the CPU baseline's sample: sequence 0, the rows its list reads
+        import numpy as np
+
+        l0, n0 = lsa.flat_select(iq[:1], pos[:1], per_seq[0], pcfg)
+        ids = l0[0, : int(n0[0])]
+        rows = torch.unique(ids[ids >= 0]).long()
+        path = os.path.join(dump["dir"], "batched.npz")
+        np.savez(path, **_np_buckets(per_seq[0]), iq=iq[:1].cpu().numpy(), pos=pos[:1].cpu().numpy(),
+                 q=q[:1].float().cpu().numpy(), k=k[:1, rows].float().cpu().numpy(),
+                 v=v[:1, rows].float().cpu().numpy(), rows=rows.cpu().numpy().astype(np.int64))
+        vis0 = min((lengths_all[0] - 1) // 512 * 8, per_seq[0].rows)
+        nbytes = (vis0 * HKV * DH * 2 + pcfg.top_p * pcfg.bucket_cap * 4 + int(n0[0]) * HKV * DH * 2 * 2
+                  + HQB * DH * 2 * 2)
+        dump["batched"] = (path, nbytes)
     del per_seq
-    pos = torch.tensor([L - 1 for L in lengths], dtype=torch.int32, device=dev)
     scale = DH ** -0.5
     stream = torch.cuda.Stream(dev)
     hkv_r = h1 - h0
+    gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
+
+    def select():
+        if mode == "heads":
+            return batched.head_sharded_select(iq, pos, bb, pcfg, gather)
+        return batched.batched_select(iq, pos, bb, pcfg)
 
     def step():
-        lists, lens = batched.batched_select(iq, pos, bb, pcfg)
+        lists, lens = select()
         return lsa.lsa_read(q, k, v, lists[:, None], lens[:, None], scale)
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step()
-        lists, lens = batched.batched_select(iq, pos, bb, pcfg)
+        lists, lens = select()
         stream.synchronize()
     n_ids = int(lens.long().sum().item())
-    vis = [min((L - 1) // 512 * 8, int(r)) for L, r in zip(lengths, bb.table_rows.tolist())]
-    # the selection's bytes count once per step (replicated selections are not extra work)
-    sel_bytes = sum(vis) * HKV * DH * 2 + nb * pcfg.top_p * pcfg.bucket_cap * 4 + nb * lists.shape[1] * 4
-    if by_heads and rank != 0:
+    own = lengths_all[sel0:sel1]
+    vis = [min((L - 1) // 512 * 8, int(r)) for L, r in zip(own, bb.table_rows.tolist())]
+    # the selection's bytes count once per step over the job (a replicated selection is not
+    # extra work): the rows this rank selects, except replicas beyond rank 0
+    sel_bytes = sum(vis) * HKV * DH * 2 + len(own) * pcfg.top_p * pcfg.bucket_cap * 4 + len(own) * lists.shape[1] * 4
+    if mode == "heads_replicated" and rank != 0:
         sel_bytes = 0
     step_bytes = sel_bytes + n_ids * hkv_r * DH * 2 * 2 + nb * (hkv_r * G * DH * 2 * 2 + HKV * DH * 4)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for _ in range(args.steps):
-            step()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def graph_of(fn, n):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            fn()
+            stream.synchronize()
+        with torch.cuda.graph(gr, stream=stream):
+            for _ in range(n):
+                fn()
+        return gr
+
+    graph = graph_of(step, 1)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     with torch.cuda.stream(stream):
-        graph.replay()
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
         stream.synchronize()
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
         with ClockSampler(dev.index) as clocks:
-            ev0.record(stream)
-            graph.replay()
-            ev1.record(stream)
+            evs[0].record(stream)
+            for i in range(args.steps):
+                graph.replay()
+                evs[i + 1].record(stream)
             stream.synchronize()
-    ms = ev0.elapsed_time(ev1) / args.steps
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ms = evs[0].elapsed_time(evs[-1]) / args.steps
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
     del graph
 
     def graph_ms(fn):
-        gr = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gr, stream=stream):
-            for _ in range(args.steps):
-                fn()
+        gr = graph_of(fn, args.steps)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             gr.replay()
+            if world > 1:
+                stream.synchronize()
+                torch.distributed.barrier()
             e0.record(stream)
             gr.replay()
             e1.record(stream)
             stream.synchronize()
+        del gr
         return e0.elapsed_time(e1) / args.steps
 
-    us_select = graph_ms(lambda: batched.batched_select(iq, pos, bb, pcfg)) * 1e3
+    us_select = graph_ms(select) * 1e3
     us_read = graph_ms(lambda: lsa.lsa_read(q, k, v, lists[:, None], lens[:, None], scale)) * 1e3
-    tot = torch.tensor([ms, float(step_bytes), float(nb)], device=dev, dtype=torch.float64)
+    tot = torch.tensor([ms, float(step_bytes), float(len(own) if mode != "heads_replicated" else nb)], device=dev,
+                       dtype=torch.float64)
     if world > 1:
         t_max = tot[:1].clone()
         torch.distributed.all_reduce(t_max, op=torch.distributed.ReduceOp.MAX)
         sums = tot[1:].clone()
         torch.distributed.all_reduce(sums)
         ms, all_bytes, all_seqs = float(t_max.item()), float(sums[0].item()), int(sums[1].item())
+        if mode == "heads_replicated":
+            all_seqs = B
     else:
-        all_bytes, all_seqs = float(step_bytes), nb
+        all_bytes, all_seqs = float(step_bytes), B
     hbm, tflops, peak_kind = _load_peaks()
     value = all_bytes / (ms * 1e-3) / 1e9
     # the dominant kernel: the read (persistent grid from 16 (row, KV head) units up)
@@ -694,19 +845,22 @@ def run_batched(args, rank, world, dev):
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": f"synthetic (seeded N(0,1) q/k/v, lengths U[{len_lo}, {len_hi}])",
-        "config": {"workload": "batched128k", "batch": B, "sequences_per_rank": nb, "heads_q": HQB,
-                   "heads_kv": HKV, "heads_kv_per_rank": hkv_r, "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"],
-                   "budget_tokens": BATCH_CFG["top_k"],
+        "config": {"workload": "batched128k", "batch": B, "sequences_selected_per_rank": len(own),
+                   "sequences_read_per_rank": nb, "heads_q": HQB, "heads_kv": HKV, "heads_kv_per_rank": hkv_r,
+                   "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"], "budget_tokens": BATCH_CFG["top_k"],
                    "lengths": [len_lo, len_hi],
-                   "parallelism": f"{'kv-head' if by_heads else 'sequence'}-shard{world}",
+                   "parallelism": {"heads": f"kv-head-shard{world} (selection split + NCCL all-gather of the lists)",
+                                   "heads_replicated": f"kv-head-shard{world} (selection replicated)",
+                                   "sequences": f"sequence-shard{world}"}[mode],
                    "l2": "no flush: one step reads > 1 GB of K/V"},
         "us_per_step": round(ms * 1e3, 2), "us_select": round(us_select, 2), "us_read": round(us_read, 2),
+        "timing": {**_dist(per_step), "note": "per step, rank 0"},
         "sequences": all_seqs, "bytes_per_step": int(all_bytes),
-        # per step: the read, and the selection - one launch, or two (streaming scorer + per-row
-        # finish) when the widest row has more than 1024 buckets (more than one cluster)
         "roofline": roof,
-        "gpu_launches": args.steps * (1 + (2 if bb.max_rows > 1024 or nb * bb.max_rows >= 8192 else 1)),
-        "step_roofline_frac": round(value / world / hbm, 4), "peak_kind": peak_kind,
+        # per step: the selection - one launch, or two (streaming scorer + per-row finish) when
+        # the widest row has more than 1024 buckets - and the read
+        "gpu_launches": args.steps * (1 + (2 if bb.max_rows > 1024 or len(own) * bb.max_rows >= 8192 else 1)),
+        "step_roofline_frac": round(value / (world * hbm), 4), "peak_kind": peak_kind,
         "clocks": clocks.summary(),
     }
 
@@ -719,15 +873,17 @@ TREE_CFG = dict(cluster_block_size=1024, pool_size=8, bucket_size=128, bucket_ca
                 beam_width=64)
 
 
-def run_tree1m(args, rank, world, dev):
+def run_tree1m(args, rank, world, dev, dump=None):
     """cfg 5: B = 4 sequences of 1,048,576 tokens, Hq 32 / Hkv 8 / Dh 128, bf16, drift keys,
     128-token buckets (8 per 1024-token block), nodes of 16 buckets, two levels, beam 64,
     top-64 buckets (8192-token budget), window 128, sinks 4; pools of 8 (a 1024-token block
     of pools of 4 would exceed the Ward merge's 128 pools). Each rank holds a contiguous,
     block-aligned 1/N of every sequence and its shard index; a step decodes one token per
     sequence through lsa_b200.seqshard (candidate all-gather, best-first merge, partial
-    reads, log-sum-exp merge over NCCL). Total work fixed -> "strong". Eager launches and
-    collectives, timed with CUDA events, max over ranks."""
+    reads, log-sum-exp merge over NCCL). Total work fixed -> "strong". Two independent sets
+    of queries and caches alternate step by step, so a step's ~136 MB of listed K/V rows is
+    not left in L2 by the step before. Each set's step is one CUDA graph (holding the NCCL
+    all-gathers when N > 1), timed with CUDA events, max over ranks."""
     import torch
 
     import lsa_b200 as lsa
@@ -738,65 +894,93 @@ def run_tree1m(args, rank, world, dev):
     pcfg = lsa.PortConfig(**TREE_CFG)
     s0, s1 = seqshard.shard_bounds(C, world, rank, TREE_CFG["cluster_block_size"])
     n = s1 - s0
-    g = torch.Generator(device=dev)
-    g.manual_seed(SEED + 5 + rank)
-    q = torch.randn(B, 1, HQ, DH, generator=g, device=dev).to(torch.bfloat16)
-    k = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
-    v = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
     gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
-    shards = []
-    for b in range(B):
-        k[b] = synthetic.drift_keys(n, HKV, DH, g, dev)[0].to(torch.bfloat16)
-        v[b] = torch.randn(n, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
-        si = seqshard.build_shard_index(index_keys(k[b]), s0, pcfg)
-        rows = gather(torch.tensor([si.buckets.rows], dtype=torch.int64, device=dev))[:, 0].tolist()
-        mine = seqshard.local_global_members(si)
-        padded = torch.full((max(rows), mine.shape[1]), -1, dtype=torch.int32, device=dev)
-        padded[: mine.shape[0]] = mine
-        tables = gather(padded)
-        si.bucket_offset = sum(rows[:rank])
-        si.members_global = torch.cat([tables[r][: rows[r]] for r in range(len(rows))]).contiguous()
-        shards.append(si)
-    # a 1-GPU run holds the whole sequence: its queries decode the last position
-    iq = [index_queries(q[b], HKV) for b in range(B)]
     pos = torch.full((1,), C - 1, dtype=torch.int32, device=dev)
     scale = DH ** -0.5
+    sets = []
+    for which in range(2):
+        g = torch.Generator(device=dev)
+        g.manual_seed(SEED + 5 + 100 * which + rank)
+        q = torch.randn(B, 1, HQ, DH, generator=g, device=dev).to(torch.bfloat16)
+        k = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
+        v = torch.empty(B, n, HKV, DH, dtype=torch.bfloat16, device=dev)
+        shards = []
+        for b in range(B):
+            k[b] = synthetic.drift_keys(n, HKV, DH, g, dev)[0].to(torch.bfloat16)
+            v[b] = torch.randn(n, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
+            si = seqshard.build_shard_index(index_keys(k[b]), s0, pcfg)
+            rows = gather(torch.tensor([si.buckets.rows], dtype=torch.int64, device=dev))[:, 0].tolist()
+            mine = seqshard.local_global_members(si)
+            padded = torch.full((max(rows), mine.shape[1]), -1, dtype=torch.int32, device=dev)
+            padded[: mine.shape[0]] = mine
+            tables = gather(padded)
+            si.bucket_offset = sum(rows[:rank])
+            si.members_global = torch.cat([tables[r][: rows[r]] for r in range(len(rows))]).contiguous()
+            shards.append(si)
+        # a 1-GPU run holds the whole sequence: its queries decode the last position
+        iq = [index_queries(q[b], HKV) for b in range(B)]
+        sets.append((q, k, v, iq, shards))
 
-    def step():  # all sequences' candidates in one all-gather, one partial read, all partials in a second
+    if dump is not None and world == 1:  # the CPU baseline's sample: sequence 0 of set 0, its list's rows
+        import numpy as np
+
+        q0, k0, v0, iq0, sh0 = sets[0]
+        si = sh0[0]
+        l0, n0 = lsa.tree_select(iq0[0], pos, si.buckets, si.hierarchy, pcfg)
+        ids = l0[0, : int(n0[0])]
+        rows = torch.unique(ids[ids >= 0]).long()
+        lv = {}
+        for i, level in enumerate(si.hierarchy.levels):
+            lv[f"lc{i}"] = level.centroids.float().cpu().numpy()
+            lv[f"lk{i}"] = level.children.cpu().numpy().astype(np.int64)
+            lv[f"ls{i}"] = level.key_sums.float().cpu().numpy()
+        path = os.path.join(dump["dir"], "tree.npz")
+        np.savez(path, **_np_buckets(si.buckets), **lv, nlev=np.int64(len(si.hierarchy.levels)),
+                 iq=iq0[0].cpu().numpy(), pos=pos.cpu().numpy(), q=q0[:1].float().cpu().numpy(),
+                 k=k0[:1, rows].float().cpu().numpy(), v=v0[:1, rows].float().cpu().numpy(),
+                 rows=rows.cpu().numpy().astype(np.int64))
+        dump["tree"] = path
+
+    def step(which):  # all sequences' candidates in one all-gather, one partial read, all partials in a second
+        q, k, v, iq, shards = sets[which]
         return seqshard.seqshard_decode_batch(q, k, v, iq, pos, shards, pcfg, gather, scale)
 
     for _ in range(args.warmup):
-        step()
+        step(0)
+        step(1)
     torch.cuda.synchronize(dev)
-    # one step captured in a CUDA graph (the step is a chain of small launches: replaying it
-    # removes the host's launch overhead); with several ranks the graph holds the two NCCL
-    # all-gathers too (measured at 2 GPUs: 365 us/step in the graph against 1008 us eager)
+    # each set's step captured in a CUDA graph (the step is a chain of small launches:
+    # replaying removes the host's launch overhead); with several ranks the graph holds the
+    # two NCCL all-gathers too
     use_graph = not args.tree_eager
-    graph = None
+    graphs = [None, None]
+    stream = torch.cuda.Stream(dev)
     if use_graph:
-        stream = torch.cuda.Stream(dev)
         stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(stream):
-            step()
-            stream.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                step()
+            for which in range(2):
+                step(which)
+                stream.synchronize()
+                graphs[which] = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graphs[which], stream=stream):
+                    step(which)
         torch.cuda.synchronize(dev)
     if world > 1:
         torch.distributed.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clocks:
-        ev0.record()
-        for _ in range(args.steps):
-            if graph is not None:
-                graph.replay()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with torch.cuda.stream(stream), ClockSampler(dev.index) as clocks:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            if graphs[i % 2] is not None:
+                graphs[i % 2].replay()
             else:
-                step()
-        ev1.record()
-        torch.cuda.synchronize(dev)
-    ms = ev0.elapsed_time(ev1) / args.steps
-    del graph  # a graph holding NCCL calls goes before the process group does
+                step(i % 2)
+            evs[i + 1].record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize(dev)
+    ms = evs[0].elapsed_time(evs[-1]) / args.steps
+    per_step = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    del graphs  # a graph holding NCCL calls goes before the process group does
     if world > 1:
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -804,7 +988,7 @@ def run_tree1m(args, rank, world, dev):
     # algorithmic bytes of a step over all ranks: listed K/V rows + scored centroids (beam)
     width_ids = TREE_CFG["top_k"] + TREE_CFG["window_size"] + TREE_CFG["sink_size"]
     kv_bytes = B * width_ids * HKV * DH * 2 * 2
-    levels_rows = sum(lv.centroids.shape[0] for si in shards for lv in si.hierarchy.levels)
+    levels_rows = sum(lv.centroids.shape[0] for si in sets[0][4] for lv in si.hierarchy.levels)
     cand_bytes = B * (TREE_CFG["beam_width"] * TREE_CFG["node_bucket_size"] * 2 + TREE_CFG["node_cluster_block_size"])
     cand_bytes *= HKV * DH * 4 * world
     step_bytes = kv_bytes + cand_bytes
@@ -817,45 +1001,101 @@ def run_tree1m(args, rank, world, dev):
         "data": "synthetic (seeded drift keys, N(0,1) q/v)",
         "config": {"workload": "tree1m", "batch": B, "context": C, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
                    "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": "NCCL all-gather x2/step (candidates, partials)",
-                   "cuda_graph": use_graph,
+                   "cuda_graph": use_graph, "rotation": "2 query/cache sets alternate step by step",
                    **{k2: TREE_CFG[k2] for k2 in ("bucket_size", "top_p", "top_k", "beam_width")},
-                   "l2": "no flush: 4 x 1M-token caches (16 GiB) >> L2"},
-        "effective_gbs": round(value, 2), "step_roofline_frac": round(value / world / hbm, 4),
+                   "l2": "no flush: 2 sets of 4 x 1M-token caches (32 GiB) >> L2, consecutive steps read different sets"},
+        "us_per_step": round(ms * 1e3, 2), "timing": {**_dist(per_step), "note": "per step, rank 0"},
+        "effective_gbs": round(value, 2), "step_roofline_frac": round(value / (world * hbm), 4),
         "bytes_per_step": step_bytes, "hierarchy_nodes": levels_rows, "peak_kind": peak_kind,
         "clocks": clocks.summary(),
     }
 
 
-# --------------------------------------------------------------------------- CPU baseline
+# --------------------------------------------------------------------------- CPU baselines
+#
+# The CPU checker (oracle/: C + numpy, single-threaded per process) timed on this box's host
+# cores: one spawn worker per core, every worker running the same bounded sample, so the
+# rate is cores x one worker's rate. Samples are saved as .npz by the GPU legs (the index
+# built by the GPU build kernels, bit-identical to the checker's own build - the parity
+# tests pin that); the timed work is the configuration's select + read on the checker.
+# K/V of the long-context configurations (128k, 1M) are saved as the rows the row's list
+# reads (ids remapped to them), so a worker holds megabytes instead of gigabytes; the read's
+# row count and arithmetic are the configuration's.
 
 
-def _cpu_sample(payload):
-    """One worker: time select+read on the checker for `n` decode rows of one cache."""
+def _cpu_worker(payload):
+    """One worker: `n` samples of one configuration on the checker -> (seconds, n, info)."""
     import numpy as np
 
     from oracle import oracle as O
 
-    path, n = payload
-    blob = np.load(path)
-    ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
-    cfg = O.Config(**CFG)
+    kind, path, n = payload
+    blob = dict(np.load(path))
     t0 = time.perf_counter()
-    length = 0
+    info = 0
     for _ in range(n):
-        lists, lengths = O.flat_select(blob["iq"], np.array([T_CTX - 1]), ob, cfg)
-        O.sparse_read(blob["q"], blob["k"], blob["v"], lists[None], lengths[None], DH ** -0.5)
-        length = int(lengths[0])
-    return time.perf_counter() - t0, n, length
+        if kind == "cfg1":  # the whole decode on the checker, ctx 2048 fp32
+            cfg = O.Config(**CFG1)
+            ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
+            lists, lengths = O.flat_select(blob["iq"], blob["pos"], ob, cfg, score_dtype="fp32")
+            O.sparse_read(blob["q"], blob["k"], blob["v"], lists[None], lengths[None], blob["scale"].item())
+            info = int(lengths[0])
+        elif kind == "decode32k":
+            ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
+            lists, lengths = O.flat_select(blob["iq"], np.array([T_CTX - 1]), ob, O.Config(**CFG))
+            O.sparse_read(blob["q"], blob["k"], blob["v"], lists[None], lengths[None], DH ** -0.5)
+            info = int(lengths[0])
+        elif kind == "prefill":  # the select of every tile, then the read of one tile's rows
+            cfg = O.Config(**CFG)
+            ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
+            tl, tn = O.tile_select(blob["iq"], ob, cfg, 64)
+            t = int(blob["tile"])
+            rl, rn = O.prefill_row_lists(tl, tn, (t + 1) * 64, cfg, 64)
+            O.sparse_read(blob["q"], blob["k"], blob["v"], rl[None, t * 64:], rn[None, t * 64:], DH ** -0.5)
+            info = int(rn[t * 64:].sum())
+        elif kind in ("batched", "tree"):
+            cfg = O.Config(**(BATCH_CFG if kind == "batched" else TREE_CFG))
+            ob = O.Buckets(blob["cf"], blob["cb"], blob["members"], blob["sizes"], blob["sums"])
+            if kind == "batched":
+                lists, lengths = O.flat_select(blob["iq"], blob["pos"], ob, cfg)
+            else:
+                levels = [O.Level(blob[f"lc{i}"], blob[f"lk{i}"], blob[f"ls{i}"]) for i in range(int(blob["nlev"]))]
+                lists, lengths = O.tree_select(blob["iq"], blob["pos"], ob, O.Hierarchy(levels), cfg)
+            # the read over the saved rows: ids remapped to their row in the saved K/V
+            rows = blob["rows"]
+            local = np.where(lists >= 0, np.searchsorted(rows, np.maximum(lists, 0)), -1).astype(np.int32)
+            O.sparse_read(blob["q"], blob["k"], blob["v"], local[None], lengths[None], DH ** -0.5)
+            info = int(lengths[0])
+    return time.perf_counter() - t0, n, info
+
+
+def _pool_rate(kind, path, seconds=8.0, cores=None):
+    """Time `kind` on every host core for about `seconds`: (samples per second, cores, info, s/sample)."""
+    import multiprocessing as mp
+
+    cores = cores or os.cpu_count() or 1
+    dt1, _, info = _cpu_worker((kind, path, 1))  # one sample in this process: the per-worker size
+    per_worker = max(1, int(seconds / max(dt1, 1e-3)))
+    ctx = mp.get_context("spawn")  # this process holds a CUDA context: never fork it
+    with ctx.Pool(cores) as pool:
+        pool.map(_cpu_worker, [(kind, path, 1)] * cores)  # imports and first touches, untimed
+        res = pool.map(_cpu_worker, [(kind, path, per_worker)] * cores)
+    # the workers run side by side: samples over the slowest worker's compute time (the
+    # sample's file load is outside each worker's clock)
+    n = sum(r[1] for r in res)
+    return n / max(r[0] for r in res), cores, info, dt1
+
+
+def _np_buckets(b):
+    return dict(cf=b.centroids_f32.cpu().numpy(), cb=b.centroids.float().cpu().numpy(), members=b.members.cpu().numpy(),
+                sizes=b.sizes.cpu().numpy(), sums=b.key_sums.cpu().numpy())
 
 
 def _dump_layer_for_cpu(L, path):
     import numpy as np
 
-    b = L["buckets"]
-    np.savez(path, cf=b.centroids_f32.cpu().numpy(), cb=b.centroids.float().cpu().numpy(),
-             members=b.members.cpu().numpy(), sizes=b.sizes.cpu().numpy(), sums=b.key_sums.cpu().numpy(),
-             iq=L["iq"].float().cpu().numpy(), q=L["q"].float().cpu().numpy(), k=L["k"].float().cpu().numpy(),
-             v=L["v"].float().cpu().numpy())
+    np.savez(path, **_np_buckets(L["buckets"]), iq=L["iq"].float().cpu().numpy(), q=L["q"].float().cpu().numpy(),
+             k=L["k"].float().cpu().numpy(), v=L["v"].float().cpu().numpy())
 
 
 def _bytes_per_select_read(length: int) -> int:
@@ -866,87 +1106,113 @@ def _bytes_per_select_read(length: int) -> int:
             + HQ * DH * 2 * 2 + HKV * DH * 2 + width * 4 * 2)
 
 
-def cpu_baseline(layer, seconds=10.0):
-    """The checker's select+read on this box's host, single core: a bounded sample."""
-    import tempfile
+def cpu_baseline(path, seconds=10.0):
+    """cfg 2 on the checker, every host core: the B200 line's cpu_baseline."""
+    rate, cores, length, dt1 = _pool_rate("decode32k", path, seconds)
+    return {"value": round(rate * _bytes_per_select_read(length) / 1e9, 4), "unit": "GB/s", "cores": cores,
+            "kind": "port", "cpu_model": _lscpu_model(),
+            "sample": f"decode32k select+read on the checker (oracle/, C + numpy), one spawn worker per core, "
+                      f"{dt1 * 1e3:.1f} ms per select+read per worker, {rate:.2f} select+reads/s in all"}
 
-    with tempfile.TemporaryDirectory() as tmp:
-        path = os.path.join(tmp, "layer0.npz")
-        _dump_layer_for_cpu(layer, path)
-        dt, n, _ = _cpu_sample((path, 1))
-        reps = max(1, min(64, int(seconds / max(dt, 1e-3))))
-        dt, n, length = _cpu_sample((path, reps))
-    per = dt / n
-    return {"value": round(_bytes_per_select_read(length) / per / 1e9, 4), "unit": "GB/s", "cores": 1,
-            "kind": "port",
-            "sample": f"{n} decode select+read on one 32k cache (oracle/, C + numpy), {per * 1e3:.2f} ms each"}
+
+CFG1 = dict(cluster_block_size=64, pool_size=4, bucket_size=64, bucket_cap=64, top_p=8, top_k=512, window_size=64,
+            sink_size=0)
+
+
+def _cfg1_sample(path):
+    """cfg 1 (the reference's CPU-runnable case): ctx 2048, Hq 8 / Hkv 2 / Dh 64, fp32,
+    64-token buckets, top-8 + the most recent bucket as the window; the index is built by
+    the checker."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    rng = np.random.default_rng(SEED + 1)
+    T, H, K, D = 2048, 8, 2, 64
+    q = rng.standard_normal((1, T, H, D)).astype(np.float32)
+    k = rng.standard_normal((1, T, K, D)).astype(np.float32)
+    v = rng.standard_normal((1, T, K, D)).astype(np.float32)
+    iq, ik = O.regroup(q[0], k[0])
+    ob = O.build_buckets(ik, O.Config(**CFG1))
+    np.savez(path, cf=ob.centroids_f32, cb=ob.centroids_bf16, members=ob.members, sizes=ob.sizes, sums=ob.key_sums,
+             iq=iq[-1:], pos=np.array([T - 1], np.int32), q=q[:, -1:], k=k, v=v, scale=np.float32(D ** -0.5))
+
+
+def cpu_baselines(tmp, samples: dict) -> dict:
+    """configs 1, 3, 4, 5 on the checker (bounded samples, every host core)."""
+    out = {"cpu_model": _lscpu_model()}
+    p1 = os.path.join(tmp, "cfg1.npz")
+    _cfg1_sample(p1)
+    rate, cores, length, dt1 = _pool_rate("cfg1", p1, 4.0)
+    out["cfg1_decode2k_fp32"] = {"value": round(dt1 * 1e6, 1), "unit": "us per select+read (one core)",
+                                 "decodes_per_s": round(rate, 1), "cores": cores, "keys_read": length,
+                                 "sample": "whole decode (select + read) of one query at ctx 2048 on the checker"}
+    if "prefill" in samples:
+        rate, cores, keys, dt1 = _pool_rate("prefill", samples["prefill"], 10.0)
+        # one sample = the select of all 512 tiles + the read of one tile (64 rows): per tile,
+        # a 512th of the select plus one tile's read
+        out["cfg3_prefill32k"] = {"value": round(64 * rate, 1), "unit": "tok/s (lower estimate: the select of "
+                                  "all 512 tiles is repeated in every 64-row sample)", "cores": cores,
+                                  "sample": "tile select of all 512 tiles + the read of one 64-row tile per sample "
+                                            f"({dt1:.2f} s per sample per worker); tok/s = 64 x samples/s"}
+    if "batched" in samples:
+        path, nbytes = samples["batched"]
+        rate, cores, length, dt1 = _pool_rate("batched", path, 8.0)
+        out["cfg4_batched128k"] = {"value": round(rate * nbytes / 1e9, 4), "unit": "GB/s", "cores": cores,
+                                   "sequences_per_s": round(rate, 2),
+                                   "sample": f"one 128k sequence's select + read (top-64, {length} ids, 8 KV heads) "
+                                             f"per sample, {dt1 * 1e3:.1f} ms per worker"}
+    if "tree" in samples:
+        path = samples["tree"]
+        rate, cores, length, dt1 = _pool_rate("tree", path, 8.0)
+        out["cfg5_tree1m"] = {"value": round(4 / rate * 1e6, 1), "unit": "us per step (4 sequences, all cores)",
+                              "cores": cores, "sample": f"one 1M-token sequence's tree select (2 levels, beam 64) + "
+                              f"read of {length} ids per sample, {dt1 * 1e3:.1f} ms per worker; a step = 4 sequences"}
+    return out
 
 
 def run_reference(args, rank, world):
     """--impl reference: the CPU path of the reference for this workload, all host cores.
 
-    The index is built on the GPU when one is visible (bit-identical to the checker's own
-    build, which the parity tests pin), else by the checker; only select+read is timed."""
+    The checker builds the index (oracle.build_buckets) and runs the select + read; this
+    process loads no CUDA library of this repository. Same config as the B200 line."""
     if rank != 0:
         return None
-    import multiprocessing as mp
     import tempfile
 
     import numpy as np
-    import torch
 
-    cores = os.cpu_count() or 1
+    from oracle import oracle as O
+
+    O.build()
     with tempfile.TemporaryDirectory() as tmp:
         path = os.path.join(tmp, "layer0.npz")
-        if torch.cuda.is_available():
-            import lsa_b200 as lsa
-            from lsa_b200.index_space import regroup_rows
-            from lsa_b200.synthetic import drift_keys
-
-            dev = torch.device("cuda:0")
-            gen = torch.Generator(device=dev)
-            gen.manual_seed(SEED + T_CTX)
-            k = drift_keys(T_CTX, HKV, DH, gen, dev).to(torch.bfloat16)
-            v = torch.randn(1, T_CTX, HKV, DH, generator=gen, device=dev).to(torch.bfloat16)
-            q = torch.randn(1, 1, HQ, DH, generator=gen, device=dev).to(torch.bfloat16)
-            _, ik = regroup_rows(k[0], k[0])
-            buckets = lsa.build_buckets_gpu(ik, lsa.PortConfig(**CFG))
-            iq, _ = regroup_rows(q[0], k[0, -1:])
-            _dump_layer_for_cpu(dict(k=k, v=v, q=q, iq=iq.to(torch.bfloat16), buckets=buckets), path)
-        else:
-            from oracle import oracle as O
-
-            g = np.random.default_rng(SEED)
-            kk = O.bf16_round(g.standard_normal((T_CTX, HKV, DH)).astype(np.float32))
-            qq = O.bf16_round(g.standard_normal((1, HQ, DH)).astype(np.float32))
-            _, ik = O.regroup(kk, kk)
-            ob = O.build_buckets(ik, O.Config(**CFG))
-            iq, _ = O.regroup(qq, kk[-1:])
-            np.savez(path, cf=ob.centroids_f32, cb=ob.centroids_bf16, members=ob.members, sizes=ob.sizes,
-                     sums=ob.key_sums, iq=O.bf16_round(iq), q=qq[None], k=kk[None],
-                     v=O.bf16_round(g.standard_normal((1, T_CTX, HKV, DH)).astype(np.float32)))
-        dt1, _, length = _cpu_sample((path, 1))
-        per_worker = max(1, int(2.0 / max(dt1, 1e-3)))  # about 2 s of work per worker per step
-        ctx = mp.get_context("spawn")
-        with ctx.Pool(cores) as pool:
-            samples = []
-            for i in range(args.warmup + args.steps):
-                t0 = time.perf_counter()
-                res = pool.map(_cpu_sample, [(path, per_worker)] * cores)
-                wall = time.perf_counter() - t0
-                if i >= args.warmup:
-                    samples.append((wall, sum(r[1] for r in res)))
-    wall = sum(w for w, _ in samples)
-    n_sr = sum(n for _, n in samples)
-    value = n_sr * _bytes_per_select_read(length) / wall / 1e9
-    ms_per_step = wall / len(samples) * 1e3
+        g = np.random.default_rng(SEED + T_CTX)
+        kk = O.bf16_round(g.standard_normal((T_CTX, HKV, DH)).astype(np.float32))
+        vv = O.bf16_round(g.standard_normal((1, T_CTX, HKV, DH)).astype(np.float32))
+        qq = O.bf16_round(g.standard_normal((1, HQ, DH)).astype(np.float32))
+        _, ik = O.regroup(kk, kk)
+        ob = O.build_buckets(ik, O.Config(**CFG))
+        iq, _ = O.regroup(qq, kk[-1:])
+        np.savez(path, cf=ob.centroids_f32, cb=ob.centroids_bf16, members=ob.members, sizes=ob.sizes, sums=ob.key_sums,
+                 iq=O.bf16_round(iq), q=qq[None], k=kk[None], v=vv)
+        cores = os.cpu_count() or 1
+        samples, lengths = [], 0
+        for i in range(args.warmup + args.steps):
+            rate, cores, lengths, dt1 = _pool_rate("decode32k", path, 2.0, cores)
+            if i >= args.warmup:
+                samples.append(rate)
+    rate = statistics.mean(samples)
+    value = rate * _bytes_per_select_read(lengths) / 1e9
+    ms_per_step = LAYERS / rate * 1e3  # a step of the B200 line: LAYERS select+reads
     return {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded)", "config": {"workload": "decode32k", "select_impl": "reference-cpu"},
+            "data": "synthetic (seeded drift keys, N(0,1) q/v)", "config": decode_config(world),
             "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                             "sample": f"{per_worker} decode select+read per worker per step, {cores} spawn "
-                                       "workers, oracle/ (C + numpy)"},
+                             "cpu_model": _lscpu_model(),
+                             "sample": f"about 2 s of decode32k select+reads per worker per step, {cores} spawn "
+                                       "workers, oracle/ (C + numpy), index built by the checker"},
             "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -975,8 +1241,10 @@ def main() -> int:
     parser.add_argument("--batched-seqs", type=int, default=64, help="batched128k sequences (profiling: fewer)")
     parser.add_argument("--batched-len", default="65536,131072",
                         help="batched128k sequence length range min,max (profiling: shorter)")
-    parser.add_argument("--batched-shard", default="heads", choices=["heads", "sequences"],
-                        help="batched128k over ranks: by KV head (selection replicated) or by sequence")
+    parser.add_argument("--batched-shard", default="heads", choices=["heads", "heads_replicated", "sequences"],
+                        help="batched128k over ranks: by KV head with the selection split (default) or "
+                             "replicated, or by sequence")
+    parser.add_argument("--no-sharded", action="store_true", help="skip the batched128k / tree1m legs")
     args = parser.parse_args()
     args.warmup = max(args.warmup, 3)
     LAYERS = args.layers
@@ -997,39 +1265,60 @@ def main() -> int:
     if world > 1:
         import datetime
 
-        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
-            os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the one JSON line
-
+        # communicator set-up lines (ranks, devices, transports) on stderr; stdout keeps the
+        # one JSON line
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    if args.workload in ("batched128k", "tree1m"):
-        out = (run_batched if args.workload == "batched128k" else run_tree1m)(args, rank, world, dev)
-        if rank == 0:
-            print(json.dumps(out), flush=True)
+
+    def finish(out):
         if world > 1:
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
+        if rank == 0 and out is not None:
+            print(json.dumps(out), flush=True)
         return 0
+
+    if args.workload in ("batched128k", "tree1m"):
+        return finish((run_batched if args.workload == "batched128k" else run_tree1m)(args, rank, world, dev))
     if args.only_prefill:
-        if rank == 0:
-            print(json.dumps(run_prefill(args, dev)), flush=True)
-        if world > 1:
-            torch.distributed.destroy_process_group()
-        return 0
-    result, layers = run_b200(args, rank, world, dev)
+        return finish(run_prefill(args, dev) if rank == 0 else None)
+    import tempfile
+
+    tmp = tempfile.TemporaryDirectory()
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline and not args.quick
+    dump = {"dir": tmp.name} if want_cpu else None
+    try:
+        result, layers = run_b200(args, rank, world, dev)
+    except GateError as e:
+        print(f"bench: refusing to report: {e}", file=sys.stderr, flush=True)
+        return 3
+    if want_cpu:
+        _dump_layer_for_cpu(layers[0], os.path.join(tmp.name, "layer0.npz"))
+    del layers
+    torch.cuda.empty_cache()
     if args.prefill_T > 0 and rank == 0 and world == 1:
-        del layers[1:]  # free the rotation's caches before the prefill leg
+        result["prefill"] = run_prefill(args, dev, dump)
         torch.cuda.empty_cache()
-        result["prefill"] = run_prefill(args, dev)
-    if rank == 0:
-        if not args.no_cpu_baseline and not args.quick and world == 1:
-            result["cpu_baseline"] = cpu_baseline(layers[0])
-        else:
-            result["cpu_baseline"] = None
-        print(json.dumps(result), flush=True)
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
-    return 0
+    if not args.no_sharded and not args.quick:
+        # the configurations that shard, on every GPU count (their scaling rides in this line)
+        result["sharded"] = {"batched128k": run_batched(args, rank, world, dev, dump=dump)}
+        torch.cuda.empty_cache()
+        if world > 1:
+            result["sharded"]["batched128k_heads_replicated"] = run_batched(args, rank, world, dev,
+                                                                            mode="heads_replicated")
+            torch.cuda.empty_cache()
+        result["sharded"]["tree1m"] = run_tree1m(args, rank, world, dev, dump=dump)
+        torch.cuda.empty_cache()
+    result["cpu_baseline"] = None
+    if want_cpu:
+        result["cpu_baseline"] = cpu_baseline(os.path.join(tmp.name, "layer0.npz"))
+        result["cpu_baselines"] = cpu_baselines(tmp.name, dump)
+    tmp.cleanup()
+    lsa_check = __import__("lsa_b200").check_status
+    lsa_check(dev, "bench")  # no bounded wait expired anywhere in the run
+    return finish(result)
 
 
 if __name__ == "__main__":

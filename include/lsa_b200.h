@@ -248,13 +248,19 @@ int lsa_sparse_read(const void* q, const void* k, const void* v, int dtype, cons
  * device memory (a server whose device memory is one arena owned by its own allocator,
  * a plugin host that forbids cudaMalloc once serving). The split partials and counters
  * live in fixed __device__ arrays of this library: at most 8 MiB of scratch and 65536
- * counters per call (lsa_sparse_read_plan reports a call's needs); larger calls return
- * LSA_ERR_SIZE and launch nothing. It calls no allocator. The first call on each device
- * resolves the arrays' addresses, so make it before any stream capture; each call zeroes
- * the counters it uses; calls share the arrays, so calls that overlap on the GPU race. */
+ * counters per call. The entry point plans without the persistent grid (so the figures of
+ * lsa_sparse_read_plan do not apply to it), checks that plan against both limits itself
+ * and returns LSA_ERR_SIZE, launching nothing, for a call beyond them. It calls no
+ * allocator. The first call on each device resolves the arrays' addresses, so make it
+ * before any stream capture; each call zeroes the counters it uses; calls share the
+ * arrays, so calls that overlap on the GPU race. status (may be null): 4 bytes the device
+ * can write (device memory, or mapped pinned host memory); once the call's work on
+ * `stream` has completed it holds 0, or LSA_ERR_TIMEOUT when a bounded wait of the read
+ * expired (the output is then incomplete). */
 int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
                             const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
-                            int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream);
+                            int64_t D, int64_t width, float scale, void* out, int64_t splits, int32_t* status,
+                            cudaStream_t stream);
 
 /* Sequence-shard partial read (no reference counterpart; the read numerics are
  * read_kernel_tiled.py:41-89 restricted to this shard's keys): ids are global positions and

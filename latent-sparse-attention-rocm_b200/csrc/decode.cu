@@ -61,8 +61,10 @@ struct FusedDecodeArgs {
 };
 
 // All CTAs of the (co-resident) grid meet; false after ~1 s (status set). bar[0] counts
-// arrivals, bar[1] departures; the last CTA to leave resets both, so the words are zero
-// at rest (other kernels share the counter buffer).
+// arrivals, bar[1] departures; every CTA counts its departure - also one whose wait
+// expired - and the last to leave resets both, so the words are back at zero once every
+// CTA has passed (other kernels share the counter buffer, and the next launch must not
+// find a stale arrival count).
 __device__ bool grid_barrier(uint32_t* bar, int32_t* status) {
     __shared__ int ok;
     __syncthreads();
@@ -79,7 +81,9 @@ __device__ bool grid_barrier(uint32_t* bar, int32_t* status) {
                 break;
             }
         }
-        if (ok && atomicAdd(bar + 1, 1u) == gridDim.x - 1) {  // everyone has seen the full count
+        // departures reach gridDim.x only after every CTA has arrived: the reset cannot
+        // race a late arrival
+        if (atomicAdd(bar + 1, 1u) == gridDim.x - 1) {
             atomicExch(bar, 0u);
             atomicExch(bar + 1, 0u);
         }

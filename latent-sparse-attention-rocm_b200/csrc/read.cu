@@ -1625,16 +1625,20 @@ static int noalloc_setup(NoAllocSlot* out) {
 extern "C" {
 
 // lsa_sparse_read without caller buffers. Limits: the plan's scratch must fit 8 MiB and
-// its counters 65536 (lsa_sparse_read_plan reports both); larger calls return
-// LSA_ERR_SIZE and launch nothing. The first call on each device resolves the arrays'
-// addresses (cudaGetSymbolAddress), so make it before any stream capture. Each call
-// zeroes the counters it uses (cudaMemsetAsync) and then launches the read; calls share
-// the arrays, so calls that overlap on the GPU (different streams, or devices sharing a
-// context) race and must be serialised by the caller.
+// its counters 65536, checked here against the plan this entry uses (no persistent grid);
+// larger calls return LSA_ERR_SIZE and launch nothing. The first call on each device
+// resolves the arrays' addresses (cudaGetSymbolAddress), so make it before any stream
+// capture. Each call zeroes the counters it uses (cudaMemsetAsync) and then launches the
+// read; calls share the arrays, so calls that overlap on the GPU (different streams, or
+// devices sharing a context) race and must be serialised by the caller. The read's status
+// word (0, or LSA_ERR_TIMEOUT after an expired bounded wait) lives in the shared counters
+// and the next call's zeroing would erase it, so it is copied (cudaMemcpyAsync, 4 bytes,
+// on `stream`) to the caller's `status` when one is given.
 int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dtype, const int32_t* ids,
                             const int32_t* lengths, int64_t B, int64_t Tq, int64_t Tk, int64_t Hq, int64_t Hkv,
-                            int64_t D, int64_t width, float scale, void* out, int64_t splits, cudaStream_t stream) {
-    if (Hkv <= 0 || Hq % Hkv || width < 0 || D <= 0) return LSA_ERR_ARG;
+                            int64_t D, int64_t width, float scale, void* out, int64_t splits, int32_t* status,
+                            cudaStream_t stream) {
+    if (Hkv <= 0 || Hq % Hkv || width < 0 || D <= 0 || B < 0 || Tq < 0) return LSA_ERR_ARG;
     // the fixed arrays take the cluster / ticket plans only (the persistent plan's split
     // partials can outgrow them)
     lsa::ReadPlan p = lsa::plan_read(B * Tq, Hkv, Hq / Hkv, D, width, splits, lsa::num_sms(), false);
@@ -1644,9 +1648,15 @@ int lsa_sparse_read_noalloc(const void* q, const void* k, const void* v, int dty
     if (rc != LSA_OK) return rc;
     if (cudaMemsetAsync(slot.counters, 0, (size_t)p.counters * sizeof(int32_t), stream) != cudaSuccess)
         return LSA_ERR_CUDA;
-    return lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out,
-                                   slot.scratch, lsa::kNoAllocScratchBytes, slot.counters, lsa::kNoAllocCounters,
-                                   splits, stream, 0, nullptr, nullptr, false);
+    rc = lsa::sparse_read_launch(q, k, v, dtype, ids, lengths, B, Tq, Tk, Hq, Hkv, D, width, scale, out, slot.scratch,
+                                 lsa::kNoAllocScratchBytes, slot.counters, lsa::kNoAllocCounters, splits, stream, 0,
+                                 nullptr, nullptr, false);
+    if (rc != LSA_OK || status == nullptr) return rc;
+    // the status word of the launch: counters[rows * KV heads] (zeroed above, so 0 when the
+    // kernel that ran keeps no status)
+    const int32_t* word = slot.counters + B * Tq * Hkv;
+    if (cudaMemcpyAsync(status, word, sizeof(int32_t), cudaMemcpyDefault, stream) != cudaSuccess) return LSA_ERR_CUDA;
+    return LSA_OK;
 }
 
 }  // extern "C"

@@ -8,6 +8,7 @@ errors. Every operator runs hand-written CUDA kernels through the C-ABI library
 """
 
 from . import _lib, pipeline, prefill, read_kernel, read_kernel_tiled, select_fused  # noqa: F401
+from ._lib import check_status  # noqa: F401
 from .index_space import make_index_space  # noqa: F401
 from .pipeline import (  # noqa: F401
     Buckets,
@@ -29,5 +30,5 @@ from .pipeline import (  # noqa: F401
 __all__ = [
     "Buckets", "Hierarchy", "NodeLevel", "PortConfig", "best_first_keys", "build_buckets_gpu",
     "build_hierarchy_gpu", "dense_read", "flat_select", "flat_select_reference", "lsa_read",
-    "make_index_space", "position_buckets", "tree_select", "visible_counts",
+    "make_index_space", "position_buckets", "tree_select", "visible_counts", "check_status",
 ]

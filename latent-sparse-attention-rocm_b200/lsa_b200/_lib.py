@@ -9,6 +9,7 @@ kernels that use them leave them zero) are cached per (device, stream) and only 
 from __future__ import annotations
 
 import ctypes
+import os
 import pathlib
 import threading
 
@@ -52,7 +53,7 @@ SIGNATURES = {
     "lsa_position_buckets": (_INT, [_P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P]),
     "lsa_pair_to_size_workspace": (_I, [_I, _I, _I]),
     "lsa_pair_to_size": (_INT, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _P]),
-    "lsa_sparse_read_noalloc": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _I, _P]),
+    "lsa_sparse_read_noalloc": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _I, _P, _P]),
     "lsa_positional_picks": (_INT, [_P, _I, _I, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_select_batched_scratch": (_I, [_I, _I]),
     "lsa_select_batched": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _P, _P, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P,
@@ -174,3 +175,51 @@ def counters(n: int, device: torch.device) -> torch.Tensor:
         buf = torch.zeros(max(int(n), 64), dtype=torch.int32, device=device)
         _ws.counters[key] = buf
     return buf
+
+
+def _on(buf: torch.Tensor, device) -> bool:
+    if device is None:
+        return True
+    dev = torch.device(device)
+    if buf.device.type != dev.type:
+        return False
+    if dev.type != "cuda":
+        return True
+    return buf.device.index == (dev.index if dev.index is not None else torch.cuda.current_device())
+
+
+def check_status(device=None, what: str = "lsa") -> None:
+    """Raise if any call since the last check left a failure behind, and recover.
+
+    Every cached counter buffer is zero between calls (tickets of last-CTA merges, barrier
+    words, the status word of a bounded wait); a kernel whose bounded wait expired writes
+    LSA_ERR_TIMEOUT (-3) into its status word and may leave a ticket counted. So at a point
+    where the device is idle, any non-zero word is a failure: this synchronises ``device``
+    (all devices with cached buffers when None), zeroes every such buffer so the next call
+    starts clean, and raises RuntimeError (timeout when a -3 word was found). Graph users
+    call it after replays; with LSA_CHECK_STATUS=1 every entry point calls it after its
+    launch (outside stream capture)."""
+    bufs = [b for b in list(_ws.counters.values()) + list(_ws.status.values()) if _on(b, device)]
+    for d in {b.device for b in bufs if b.device.type == "cuda"}:
+        torch.cuda.synchronize(d)
+    timed_out, dirty = False, False
+    for b in bufs:
+        bad = b != 0
+        if bool(bad.any()):
+            dirty = True
+            timed_out = timed_out or bool((b == ERR_TIMEOUT).any())
+            b.zero_()
+    if timed_out:
+        raise RuntimeError(f"{what}: a bounded device wait expired (LSA_ERR_TIMEOUT); counters reset")
+    if dirty:
+        raise RuntimeError(f"{what}: device counters were not at rest after the call; counters reset")
+
+
+def after_call(device: torch.device, what: str) -> None:
+    """The checked mode (LSA_CHECK_STATUS=1, read per call): synchronise and raise on a
+    failure word right after the launch - skipped while a CUDA graph is being captured."""
+    if os.environ.get("LSA_CHECK_STATUS", "0") != "1":
+        return
+    if torch.cuda.is_current_stream_capturing():
+        return
+    check_status(device, what)

@@ -60,6 +60,7 @@ def tree_picks(index_queries, positions, buckets, hierarchy, config) -> torch.Te
                             buckets.rows, n, cptrs, kptrs, counts, ptr(bc), config.node_bucket_size,
                             config.node_cluster_block_size, config.top_level, config.beam_width, config.top_p,
                             ptr(picks), ptr(sc), sc.numel(), ptr(ct), ct.numel(), stream_of(q)), "tree_select")
+    _lib.after_call(dev, "tree_select")
     return picks
 
 

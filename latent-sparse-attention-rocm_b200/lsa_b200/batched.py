@@ -90,6 +90,7 @@ def batched_select(index_queries, positions, bb: BatchedBuckets, config, top_k=N
                                bb.members.shape[1], config.top_p, config.window_size, config.sink_size, top_k,
                                ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct), ct.numel(), -1, stream_of(q)),
           "batched_select")
+    _lib.after_call(dev, "batched_select")
     return lists, lengths
 
 
@@ -97,6 +98,18 @@ def batched_decode(q, k, v, index_queries, positions, bb: BatchedBuckets, config
     """Select + read for one decoded token per sequence: q [B, 1, Hq, Dh] -> out like q."""
     lists, lengths = batched_select(index_queries, positions, bb, config)
     return pipeline.lsa_read(q, k, v, lists[:, None], lengths[:, None], scale)
+
+
+def head_sharded_select(index_queries, positions, bb: BatchedBuckets, config, gather, top_k=None):
+    """Head sharding without a replicated selection: this rank selects only its share of
+    the sequences (``bb`` / ``index_queries`` / ``positions`` hold that share, equal shares
+    on every rank), and one all-gather hands every rank every sequence's read list - the
+    rank then reads its own KV heads of all sequences. ``gather`` maps x [...] to
+    [world, ...] (``seqshard.all_gather_fn()`` over NCCL). Returns (lists [B, width],
+    lengths [B]) with B = world x this rank's share, in rank order."""
+    lists, lengths = batched_select(index_queries, positions, bb, config, top_k)
+    all_lists, all_lengths = gather(lists), gather(lengths)
+    return all_lists.reshape(-1, lists.shape[-1]), all_lengths.reshape(-1)
 
 
 def shard_rows(B: int, world: int, rank: int) -> tuple[int, int]:

@@ -46,7 +46,7 @@ SELECT_IMPLS = ("reference", "fused", "fused_unpack")
 class PortConfig:
     """The design's knobs (ref ``pipeline.py:32-54``)."""
 
-    cluster_block_size: int = 512  # = window: a block closes when the window slides past it
+    cluster_block_size: int = 512  # keys per Ward block; blocks become visible once closed
     pool_size: int = 4
     bucket_size: int = 8
     bucket_cap: int = 16
@@ -69,7 +69,7 @@ class PortConfig:
 class Buckets:
     """A cache's buckets on the GPU (ref ``pipeline.py:57-68``) plus their fp32 key sums."""
 
-    centroids: torch.Tensor  # [rows, index_dim] bf16 - what production scoring reads
+    centroids: torch.Tensor  # [rows, index_dim] bf16, the scoring operand of the selects
     members: torch.Tensor  # [rows, bucket_cap] int32, absolute positions, -1 padded
     sizes: torch.Tensor  # [rows] int32
     centroids_f32: torch.Tensor | None = None  # [rows, index_dim] fp32
@@ -378,6 +378,7 @@ def _select_fused(index_queries, positions, buckets, config, top_k, score_dtype)
                              ptr(buckets.members), buckets.members.shape[1], config.top_p, config.window_size,
                              config.sink_size, top_k, ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct),
                              ct.numel(), -1, stream_of(q)), "flat_select(fused)")
+    _lib.after_call(dev, "flat_select(fused)")
     return lists, lengths
 
 
@@ -450,6 +451,7 @@ def decode_fused(q, k, v, index_queries, positions, buckets, config, scale=None,
                              config.sink_size, config.top_k, ptr(qc), ptr(kc), ptr(vc), _lib.DTYPE_CODE[q.dtype], Tk,
                              Hq, Hkv, D, scale, ptr(out), ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct),
                              ct.numel(), stream_of(q)), "decode_fused")
+    _lib.after_call(dev, "decode_fused")
     return (out, lists, lengths) if return_lists else out
 
 

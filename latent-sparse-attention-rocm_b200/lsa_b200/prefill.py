@@ -66,6 +66,7 @@ def tile_select(index_queries: torch.Tensor, buckets, config, tile: int = TILE, 
                             config.cluster_block_size, config.block_bucket_count, ptr(buckets.members),
                             buckets.members.shape[1], config.top_p, config.sink_size, top_k, ptr(lists),
                             ptr(lengths), ptr(sc), sc.numel(), ptr(ct), ct.numel(), stream_of(iq)), "tile_select")
+    _lib.after_call(dev, "tile_select")
     return lists, lengths
 
 
@@ -131,6 +132,7 @@ def sparse_prefill(q, k, v, tile_lists, tile_lengths, block: int, scale=None, ti
     check(lib().lsa_sparse_prefill(ptr(q), ptr(k), ptr(v), _lib.DTYPE_CODE[q.dtype], ptr(tl), ptr(tn), tl.shape[-1],
                                    B, T, Tk, Hq, Hkv, D, tile, block, scale, ptr(out), ptr(st), stream_of(q)),
           "sparse_prefill")
+    _lib.after_call(q.device, "sparse_prefill")
     return out
 
 

@@ -48,6 +48,7 @@ def _read(q, k, v, read_ids, lengths, scale, splits: int = 0):
     check(L.lsa_sparse_read(ptr(q), ptr(k), ptr(v), _lib.DTYPE_CODE[q.dtype], ptr(ids), ptr(lens), B, Tq, Tk, Hq, Hkv,
                             D, width, scale, ptr(out), ptr(sc), sc.numel(), ptr(ct), ct.numel(), splits,
                             stream_of(q)), "sparse_read")
+    _lib.after_call(q.device, "sparse_read")
     return out
 
 

@@ -122,6 +122,7 @@ def shard_candidates(index_queries, positions, s: ShardIndex, config, local_posi
                                  config.node_cluster_block_size, config.top_level, config.beam_width, config.top_p,
                                  ptr(picks), ptr(keys), s.bucket_offset, ptr(sc), sc.numel(), ptr(ct), ct.numel(),
                                  stream_of(q)), "shard_candidates")
+    _lib.after_call(dev, "shard_candidates")
     return keys
 
 
@@ -169,6 +170,7 @@ def shard_partial_read(q, k_shard, v_shard, lists, lengths, start: int, scale=No
     check(L.lsa_sparse_read_partial(ptr(q), ptr(k_shard), ptr(v_shard), _lib.DTYPE_CODE[q.dtype], ptr(ids), ptr(lens),
                                     B, Tq, Tk, Hq, Hkv, D, width, scale, start, ptr(out), ptr(lse), ptr(sc),
                                     sc.numel(), ptr(ct), ct.numel(), 0, stream_of(q)), "shard_partial_read")
+    _lib.after_call(q.device, "shard_partial_read")
     return out, lse
 
 

@@ -20,6 +20,9 @@ for p in (str(ROOT), str(PKG)):
         sys.path.insert(0, p)
 
 SEED = 20261105
+# checked mode: every entry point synchronises after its launch and raises if a bounded
+# wait expired or a counter was left off zero (lsa_b200.check_status)
+os.environ.setdefault("LSA_CHECK_STATUS", "1")
 
 
 def pytest_configure(config):

@@ -52,3 +52,27 @@ def test_selftest_rejects_bad_limits(lsa):
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     assert _lib.lib().lsa_wait_selftest(_lib.ptr(status), 0, 1, _lib.stream_of(status)) == _lib.ERR_ARG
     assert _lib.lib().lsa_wait_selftest(_lib.ptr(status), 3_000_000_000, 1, _lib.stream_of(status)) == _lib.ERR_ARG
+
+
+def test_expired_wait_in_cached_counters_is_caught_and_reset(lsa, oracle):
+    """A timeout word left in the per-stream counter cache (where the reads, selects and
+    fused decode keep their tickets and status words) is found by check_status, which
+    raises and zeroes the cache; the next read (checked mode) runs clean and is correct."""
+    from lsa_b200 import _lib
+
+    ct = _lib.counters(64, torch.device(DEV))
+    view = ct[5:6]  # any word of the cache: the position of a status word depends on the call
+    assert _lib.lib().lsa_wait_selftest(_lib.ptr(view), 20_000_000, 0, _lib.stream_of(view)) == 0
+    with pytest.raises(RuntimeError, match="bounded device wait expired"):
+        lsa.check_status(DEV)
+    assert int(ct.abs().sum().item()) == 0
+    rng = np.random.default_rng(1)
+    q = (rng.standard_normal((1, 1, 32, 128)) * 0.3).astype(np.float32)
+    k = (rng.standard_normal((1, 512, 8, 128)) * 0.3).astype(np.float32)
+    v = rng.standard_normal((1, 512, 8, 128)).astype(np.float32)
+    ids = rng.integers(0, 512, (1, 1, 300)).astype(np.int32)
+    ln = np.array([[300]], np.int32)
+    want = oracle.sparse_read(q, k, v, ids, ln)
+    t = lambda x: torch.from_numpy(x).to(DEV)
+    got = lsa.read_kernel_tiled.sparse_read_auto(t(q), t(k), t(v), t(ids), t(ln), 128 ** -0.5)
+    assert float(np.abs(got.cpu().numpy() - want).max()) <= 1e-5
