@@ -40,6 +40,50 @@ __global__ void regroup_kernel(const T* __restrict__ q, const T* __restrict__ k,
     for (int j = lane; j < d; j += 32) ik[t * d + j] = __fdiv_rn(to_f32(row[j]), den);
 }
 
+// The same per-row arithmetic as regroup_kernel for few rows (decode): one CTA of 256
+// threads per row, every thread's query loads in flight together (elements j = tid + 256 i,
+// G group members each, summed in group order then divided by G), the key norm by warp 0
+// (the canonical warp dot), then every thread divides its elements. Requires G <= 8 and
+// d <= 2048.
+constexpr int kRegroupThreads = 256;
+template <typename T>
+__global__ void __launch_bounds__(kRegroupThreads) regroup_row_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                                      int Hq, int Hkv, int D, float* __restrict__ iq,
+                                                                      float* __restrict__ ik) {
+    __shared__ float den_s;
+    const int64_t t = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int G = Hq / Hkv, d = Hkv * D;
+    constexpr int kPer = 2048 / kRegroupThreads;
+    float qv[kPer][8];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {  // unconditional loads at clamped in-range addresses
+        const int j = min(tid + kRegroupThreads * i, d - 1);
+        const int h = j / D, e = j % D;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) qv[i][g] = to_f32(q[(t * Hq + h * G + min(g, G - 1)) * D + e]);
+    }
+    const T* row = k + t * Hkv * D;
+    if (tid < 32) {
+        const float n = __fsqrt_rn(warp_cdot<T, T>(row, row, d, tid));
+        if (tid == 0) den_s = fmaxf(n, 1e-12f);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+        const int j = tid + kRegroupThreads * i;
+        if (j < d) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+                if (g < G) acc = __fadd_rn(acc, qv[i][g]);
+            iq[t * d + j] = __fdiv_rn(acc, (float)G);
+        }
+    }
+    __syncthreads();
+    const float den = den_s;
+    for (int j = tid; j < d; j += kRegroupThreads) ik[t * d + j] = __fdiv_rn(to_f32(row[j]), den);
+}
+
 // out = x / max(|x|, 1e-12) per row (+ bf16 copy, round to nearest even), one warp per row.
 __global__ void normalize_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ out,
                                  __nv_bfloat16* __restrict__ out_bf16) {
@@ -372,6 +416,22 @@ int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, 
                 float* ik, cudaStream_t stream) {
     if (Hkv <= 0 || Hq % Hkv || (Hkv * D) % 8 || ((uintptr_t)k & 15) || (D % 8)) return LSA_ERR_ARG;
     if (T == 0) return LSA_OK;
+    if (T <= 1024 && Hq / Hkv <= 8 && Hkv * D <= 2048) {  // few rows (decode): a CTA per row
+        const unsigned rg = (unsigned)T;
+        if (dtype == kBF16)
+            regroup_row_kernel<__nv_bfloat16><<<rg, kRegroupThreads, 0, stream>>>(
+                (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (int)Hq, (int)Hkv, (int)D, iq, ik);
+        else if (dtype == kF16)
+            regroup_row_kernel<__half><<<rg, kRegroupThreads, 0, stream>>>((const __half*)q, (const __half*)k, (int)Hq,
+                                                                          (int)Hkv, (int)D, iq, ik);
+        else if (dtype == kF32)
+            regroup_row_kernel<float><<<rg, kRegroupThreads, 0, stream>>>((const float*)q, (const float*)k, (int)Hq,
+                                                                          (int)Hkv, (int)D, iq, ik);
+        else
+            return LSA_ERR_ARG;
+        LSA_LAUNCH_CHECK();
+        return LSA_OK;
+    }
     unsigned grid = nblk(T, 8);
     if (dtype == kBF16)
         regroup_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)k, T,

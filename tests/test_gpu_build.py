@@ -25,8 +25,12 @@ def _bits_equal(a, b):
 
 
 @pytest.mark.parametrize("T,Hq,Hkv,D,dtype", [(300, 8, 2, 64, torch.float32), (512, 32, 8, 128, torch.bfloat16),
-                                               (64, 12, 4, 64, torch.float16)])
+                                               (64, 12, 4, 64, torch.float16), (1, 32, 8, 128, torch.bfloat16),
+                                               (3, 16, 16, 128, torch.bfloat16), (5, 64, 4, 64, torch.float16),
+                                               (2000, 8, 2, 64, torch.float32)])
 def test_regroup_exact(oracle, lsa, T, Hq, Hkv, D, dtype):
+    """Bit-exact against the checker: one CTA per row up to 1024 rows (G <= 8, d <= 2048),
+    one warp per row beyond (and for larger groups)."""
     rng = np.random.default_rng(T)
     q = torch.from_numpy(rng.standard_normal((1, T, Hq, D)).astype(np.float32)).to(dtype)
     k = torch.from_numpy(rng.standard_normal((1, T, Hkv, D)).astype(np.float32)).to(dtype)
