@@ -3,9 +3,9 @@
 Same fixtures as tests/test_oracle_select_golden.py (tests/golden/select_golden.npz, made
 by running the reference's select_fused.py / pipeline.py / _tree.py with only the absent
 upstream names stubbed): the fused top-k (lsa_select_topk_scores), the walk from packed
-keys (lsa_expand_from_keys), best_first_keys with and without the listing mask, the
-fused one-launch select fed the fixtures' scores' inputs, and the tree beam's picks
-(lsa_tree_select) on an index the GPU builds from the fixtures' keys. Bit-exact.
+keys (lsa_expand_from_keys), best_first_keys with and without the listing mask, and the
+tree beam's picks (lsa_tree_select) on an index the GPU builds from the fixtures' keys.
+Bit-exact.
 """
 
 import pathlib
