@@ -525,9 +525,9 @@ def run_b200(args, rank, world, dev):
                 "traffic": _traffic_from_profile("fused_decode_32k.md"),
                 "bytes_per_launch": round(step_bytes / LAYERS)}
     else:
-        roof = {"bound": "hbm", "kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1),
+        roof = {"bound": "hbm", "kernel": "lsa::decode_read_kernel", "achieved": round(read_gbs, 1),
                 "peak": hbm, "unit": "GB/s", "frac": round(read_gbs / hbm, 4), "peak_kind": peak_kind,
-                "traffic": _traffic_from_profile("sparse_read_decode32k.md"),
+                "traffic": _traffic_from_profile("decode_read_32k.md"),
                 "bytes_per_launch": round(read_bytes_per_launch)}
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -540,8 +540,13 @@ def run_b200(args, rank, world, dev):
         "us_per_select_read_split": round(ms_split / args.steps / LAYERS * 1e3, 3),
         "us_per_select_read_fused": round(ms_fused / args.steps / LAYERS * 1e3, 3),
         "us_per_select": round(us_select, 3), "us_per_read": round(us_read, 3),
-        "read_roofline": {"kernel": "lsa::sparse_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
+        "read_roofline": {"kernel": "lsa::decode_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
                           "frac": round(read_gbs / hbm, 4)},
+        "select_roofline": {"kernel": "lsa::select_decode_kernel", "unit": "GB/s",
+                            "bytes_per_launch": round((centroid_bytes + members_bytes) / LAYERS),
+                            "achieved": round((centroid_bytes + members_bytes) / LAYERS / (us_select * 1e-6) / 1e9, 1),
+                            "frac": round((centroid_bytes + members_bytes) / LAYERS / (us_select * 1e-6) / 1e9 / hbm,
+                                          4)},
         "dense_us_per_decode": round(us_dense, 3),
         "batch_decode": None if ms_batch != ms_batch else {
             "sequences": LAYERS, "us_per_batch": round(ms_batch * 1e3, 2), "gbs": round(step_bytes / (ms_batch * 1e-3) / 1e9, 1),
