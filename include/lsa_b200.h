@@ -9,7 +9,9 @@
  * LSA_ERR_TIMEOUT in a device status word instead of hanging; the bucket builds record
  * LSA_ERR_SHORT there when a block cannot reach its bucket count under the cap.
  *
- * Dtype codes: 0 = fp32, 1 = fp16, 2 = bf16. "Counters" arguments are int32 device
+ * Dtype codes: 0 = fp32, 1 = fp16, 2 = bf16; the selects' query code also takes 3 = fp32
+ * storage read as its bf16 rounding (lsa_select_fused, lsa_select_batched: the bf16 scoring
+ * of an fp32 index query with no separate cast). "Counters" arguments are int32 device
  * arrays that must be zero before the call; the kernels leave them zero, so one
  * buffer serves every later call on the same stream (and CUDA-graph replays).
  * Calls sharing a scratch or counters buffer must not overlap on the GPU.

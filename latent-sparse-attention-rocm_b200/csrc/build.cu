@@ -51,6 +51,10 @@ __global__ void __launch_bounds__(kRegroupThreads) regroup_row_kernel(const T* _
                                                                       int Hq, int Hkv, int D, float* __restrict__ iq,
                                                                       float* __restrict__ ik) {
     __shared__ float den_s;
+    // launched with programmatic stream serialization (decode: right after the previous
+    // layer's read): q and k are read only after the previous kernel has completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int64_t t = blockIdx.x;
     const int tid = threadIdx.x;
     const int G = Hq / Hkv, d = Hkv * D;
@@ -417,20 +421,28 @@ int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, 
     if (Hkv <= 0 || Hq % Hkv || (Hkv * D) % 8 || ((uintptr_t)k & 15) || (D % 8)) return LSA_ERR_ARG;
     if (T == 0) return LSA_OK;
     if (T <= 1024 && Hq / Hkv <= 8 && Hkv * D <= 2048) {  // few rows (decode): a CTA per row
-        const unsigned rg = (unsigned)T;
+        cudaLaunchAttribute pdl;
+        pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        pdl.val.programmaticStreamSerializationAllowed = 1;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)T);
+        lc.blockDim = dim3(kRegroupThreads);
+        lc.stream = stream;
+        lc.attrs = &pdl;
+        lc.numAttrs = 1;
+        cudaError_t e;
         if (dtype == kBF16)
-            regroup_row_kernel<__nv_bfloat16><<<rg, kRegroupThreads, 0, stream>>>(
-                (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (int)Hq, (int)Hkv, (int)D, iq, ik);
+            e = cudaLaunchKernelEx(&lc, regroup_row_kernel<__nv_bfloat16>, (const __nv_bfloat16*)q,
+                                   (const __nv_bfloat16*)k, (int)Hq, (int)Hkv, (int)D, iq, ik);
         else if (dtype == kF16)
-            regroup_row_kernel<__half><<<rg, kRegroupThreads, 0, stream>>>((const __half*)q, (const __half*)k, (int)Hq,
-                                                                          (int)Hkv, (int)D, iq, ik);
+            e = cudaLaunchKernelEx(&lc, regroup_row_kernel<__half>, (const __half*)q, (const __half*)k, (int)Hq,
+                                   (int)Hkv, (int)D, iq, ik);
         else if (dtype == kF32)
-            regroup_row_kernel<float><<<rg, kRegroupThreads, 0, stream>>>((const float*)q, (const float*)k, (int)Hq,
-                                                                          (int)Hkv, (int)D, iq, ik);
+            e = cudaLaunchKernelEx(&lc, regroup_row_kernel<float>, (const float*)q, (const float*)k, (int)Hq, (int)Hkv,
+                                   (int)D, iq, ik);
         else
             return LSA_ERR_ARG;
-        LSA_LAUNCH_CHECK();
-        return LSA_OK;
+        return e == cudaSuccess ? LSA_OK : LSA_ERR_CUDA;
     }
     unsigned grid = nblk(T, 8);
     if (dtype == kBF16)

@@ -19,7 +19,9 @@ namespace lsa {
 
 constexpr int64_t kEmpty = INT64_MIN;  // empty packed key: sorts after every real key
 
-enum Dtype : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+// kF32AsBF16: fp32 storage read as bf16 values (rounded to nearest even on load) - the
+// selects' query code for "bf16 scoring of an fp32 index query" without a cast launch
+enum Dtype : int { kF32 = 0, kF16 = 1, kBF16 = 2, kF32AsBF16 = 3 };
 
 // ------------------------------------------------------------------ conversions
 
@@ -40,6 +42,16 @@ template <> __device__ __forceinline__ void load8<float>(const float* p, float (
     float4 b = *reinterpret_cast<const float4*>(p + 4);
     out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
     out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+
+// An fp32 element that reads as its bf16 rounding (dtype code kF32AsBF16).
+struct F32AsBF16 {
+    float v;
+};
+template <> __device__ __forceinline__ void load8<F32AsBF16>(const F32AsBF16* p, float (&out)[8]) {
+    load8<float>(reinterpret_cast<const float*>(p), out);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) out[e] = __bfloat162float(__float2bfloat16_rn(out[e]));
 }
 
 template <> __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&out)[8]) {

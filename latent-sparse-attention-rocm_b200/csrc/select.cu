@@ -1397,7 +1397,8 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
     // per-row finish when their limits hold (bf16 centroids, top_p <= 128, staged members
     // fit, 16-byte member rows, a status word)
     const bool wide_batch = R * most >= 8192;
-    if (!many_rows && (!use_cluster || wide_batch) && c_dtype == kBF16 && (q_dtype == kBF16 || q_dtype == kF32) &&
+    if (!many_rows && (!use_cluster || wide_batch) && c_dtype == kBF16 &&
+        (q_dtype == kBF16 || q_dtype == kF32 || q_dtype == kF32AsBF16) &&
         R <= kStreamMaxRows && top_p <= 128 && k * cap <= kMemberPrefetch && cap % 4 == 0 && aligned16(members) &&
         top_k <= kFinishMaxTopK && n_counters >= R + 1 && d * 2 <= kStreamStageBytes && N < (1ll << 30)) {
         // item size: up to 128 columns, smaller (whole stages) until the batch makes about two
@@ -1454,6 +1455,11 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
             else if (ch <= 2) LSA_ST(__nv_bfloat16, 2);
             else if (ch <= 4) LSA_ST(__nv_bfloat16, 4);
             else LSA_ST(__nv_bfloat16, 8);
+        } else if (q_dtype == kF32AsBF16) {
+            if (ch <= 1) LSA_ST(F32AsBF16, 1);
+            else if (ch <= 2) LSA_ST(F32AsBF16, 2);
+            else if (ch <= 4) LSA_ST(F32AsBF16, 4);
+            else LSA_ST(F32AsBF16, 8);
         } else {
             if (ch <= 1) LSA_ST(float, 1);
             else if (ch <= 2) LSA_ST(float, 2);
@@ -1516,6 +1522,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
         else LSA_DS(TQ, TC, 8);              \
     } while (0)
         if (q_dtype == kBF16 && c_dtype == kBF16) LSA_DS_CH(__nv_bfloat16, __nv_bfloat16);
+        else if (q_dtype == kF32AsBF16 && c_dtype == kBF16) LSA_DS_CH(F32AsBF16, __nv_bfloat16);
         else if (q_dtype == kF32 && c_dtype == kF32) LSA_DS_CH(float, float);
         else if (q_dtype == kF32 && c_dtype == kBF16) LSA_DS_CH(float, __nv_bfloat16);
         else return LSA_ERR_ARG;
@@ -1567,6 +1574,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
         else LSA_FS(TQ, TC, 8);          \
     } while (0)
     if (q_dtype == kBF16 && c_dtype == kBF16) LSA_FS_CH(__nv_bfloat16, __nv_bfloat16);
+    else if (q_dtype == kF32AsBF16 && c_dtype == kBF16) LSA_FS_CH(F32AsBF16, __nv_bfloat16);
     else if (q_dtype == kF32 && c_dtype == kF32) LSA_FS_CH(float, float);
     else if (q_dtype == kF32 && c_dtype == kBF16) LSA_FS_CH(float, __nv_bfloat16);
     else return LSA_ERR_ARG;

@@ -18,6 +18,7 @@ import torch
 LIB_PATH = pathlib.Path(__file__).resolve().parent / "liblsa_b200.so"
 
 F32, F16, BF16 = 0, 1, 2
+F32_AS_BF16 = 3  # selects' query code: fp32 storage read as its bf16 rounding
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
 OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_SHORT, ERR_SIZE = 0, -1, -2, -3, -4, -5

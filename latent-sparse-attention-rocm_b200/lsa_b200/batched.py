@@ -67,12 +67,9 @@ def batched_select(index_queries, positions, bb: BatchedBuckets, config, top_k=N
     top_k = config.top_k if top_k is None else int(top_k)
     if positions.shape[0] != index_queries.shape[0] or bb.table_off.shape[0] != index_queries.shape[0]:
         raise ValueError("batched_select: one index query, one position and one bucket table per sequence")
-    if score_dtype == "fp32":
-        if bb.centroids_f32 is None:
-            raise ValueError("batched_select(score_dtype='fp32') needs fp32 centroids")
-        q, c = index_queries.float().contiguous(), bb.centroids_f32
-    else:
-        q, c = index_queries.to(torch.bfloat16).contiguous(), bb.centroids
+    if score_dtype == "fp32" and bb.centroids_f32 is None:
+        raise ValueError("batched_select(score_dtype='fp32') needs fp32 centroids")
+    q, q_code, c = pipeline._scoring_operands(index_queries, bb.centroids, bb.centroids_f32, score_dtype)
     R, d = q.shape
     dev = q.device
     width = top_k + config.window_size + config.sink_size
@@ -84,7 +81,7 @@ def batched_select(index_queries, positions, bb: BatchedBuckets, config, top_k=N
     L = lib()
     sc = _lib.scratch(L.lsa_select_batched_scratch(R, bb.max_rows), dev)
     ct = _lib.counters(R + 1, dev)  # tickets + the status word
-    check(L.lsa_select_batched(ptr(q), _lib.DTYPE_CODE[q.dtype], R, d, ptr(c), _lib.DTYPE_CODE[c.dtype], d,
+    check(L.lsa_select_batched(ptr(q), q_code, R, d, ptr(c), _lib.DTYPE_CODE[c.dtype], d,
                                ptr(bb.table_off), ptr(bb.table_rows), bb.max_rows, ptr(pos),
                                config.cluster_block_size, config.block_bucket_count, ptr(bb.members),
                                bb.members.shape[1], config.top_p, config.window_size, config.sink_size, top_k,

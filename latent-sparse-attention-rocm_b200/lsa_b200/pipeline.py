@@ -350,16 +350,25 @@ def flat_select_reference(index_queries, positions, buckets, config, top_k=None,
     return expand_in_order(picked, buckets.members, positions, config.window_size, config.sink_size, top_k)
 
 
+def _scoring_operands(index_queries, centroids_bf16, centroids_f32, score_dtype):
+    """(queries, query dtype code, centroids) of a fused select: "fp32" scores fp32 queries on
+    the fp32 centroids; "bf16" scores bf16(queries) on the bf16 centroids - an fp32 query
+    goes in as is with code F32_AS_BF16 (the kernel rounds it on load: no cast launch)."""
+    if score_dtype == "fp32":
+        return index_queries.float().contiguous(), _lib.F32, centroids_f32
+    if index_queries.dtype == torch.float32:
+        return index_queries.contiguous(), _lib.F32_AS_BF16, centroids_bf16
+    q = index_queries.to(torch.bfloat16).contiguous()
+    return q, _lib.BF16, centroids_bf16
+
+
 def _select_fused(index_queries, positions, buckets, config, top_k, score_dtype):
     """One launch from index queries to read lists (``lsa_select_fused``)."""
     if positions.shape[0] != index_queries.shape[0]:
         raise ValueError(
             f"a position a query: {index_queries.shape[0]} queries, {positions.shape[0]} positions"
         )
-    if score_dtype == "fp32":
-        q, c = index_queries.float().contiguous(), buckets.centroids_f32
-    else:
-        q, c = index_queries.to(torch.bfloat16).contiguous(), buckets.centroids
+    q, q_code, c = _scoring_operands(index_queries, buckets.centroids, buckets.centroids_f32, score_dtype)
     R, d = q.shape
     N = c.shape[0]
     dev = q.device
@@ -373,7 +382,7 @@ def _select_fused(index_queries, positions, buckets, config, top_k, score_dtype)
     nbytes = L.lsa_select_fused_scratch(R, N)
     sc = _lib.scratch(nbytes, dev)
     ct = _lib.counters(R + 1, dev)  # tickets + the status word
-    check(L.lsa_select_fused(ptr(q), _lib.DTYPE_CODE[q.dtype], R, d, ptr(c.contiguous()), _lib.DTYPE_CODE[c.dtype],
+    check(L.lsa_select_fused(ptr(q), q_code, R, d, ptr(c.contiguous()), _lib.DTYPE_CODE[c.dtype],
                              N, d, ptr(pos), config.cluster_block_size, config.block_bucket_count,
                              ptr(buckets.members), buckets.members.shape[1], config.top_p, config.window_size,
                              config.sink_size, top_k, ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct),

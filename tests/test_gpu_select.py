@@ -217,3 +217,36 @@ def test_expand_staging_paths(oracle, lsa, P, cap, top_k):
     tp, tm, tpos = (torch.from_numpy(x).to(DEV) for x in (picks, members, pos))
     got_l, got_n = lsa.pipeline.expand_in_order(tp, tm, tpos, 64, 4, top_k)
     assert (_np(got_l) == want_l).all() and (_np(got_n) == want_n).all()
+
+
+@pytest.mark.parametrize("R,N,top_p,cap,d", [(1, 504, 32, 128, 1024), (3, 40, 8, 32, 128), (2, 1500, 64, 64, 256),
+                                             (40, 300, 16, 16, 128)])
+def test_fp32_queries_read_as_bf16_equal_cast_queries(lsa, R, N, top_p, cap, d):
+    """Query code 3 (fp32 storage, rounded to bf16 on load) gives byte-identical lists to the
+    same queries cast to bf16 first (code 2), on the decode, cluster, streaming and per-row
+    paths of lsa_select_fused."""
+    from lsa_b200 import _lib
+
+    rng = np.random.default_rng(N + top_p)
+    block, bpb = 512, 8
+    T = (N // bpb + 1) * block
+    c = torch.from_numpy(rng.standard_normal((N, d)).astype(np.float32)).to(DEV).bfloat16()
+    members = torch.from_numpy(rng.integers(-1, T, (N, cap)).astype(np.int32)).to(DEV)
+    q32 = torch.from_numpy(rng.standard_normal((R, d)).astype(np.float32)).to(DEV)
+    pos = torch.from_numpy(rng.integers(T // 2, T, R).astype(np.int32)).to(DEV)
+    top_k, window, sink = 4 * cap, 64, 4
+    width = top_k + window + sink
+    L = _lib.lib()
+    outs = []
+    for q, code in ((q32, _lib.F32_AS_BF16), (q32.bfloat16().contiguous(), _lib.BF16)):
+        lists = torch.empty(R, width, dtype=torch.int32, device=DEV)
+        lengths = torch.empty(R, dtype=torch.int32, device=DEV)
+        sc = torch.empty(L.lsa_select_fused_scratch(R, N) + 256, dtype=torch.uint8, device=DEV)
+        ct = torch.zeros(R + 1, dtype=torch.int32, device=DEV)
+        rc = L.lsa_select_fused(_lib.ptr(q), code, R, d, _lib.ptr(c), _lib.BF16, N, d, _lib.ptr(pos), block, bpb,
+                                _lib.ptr(members), cap, top_p, window, sink, top_k, _lib.ptr(lists),
+                                _lib.ptr(lengths), _lib.ptr(sc), sc.numel(), _lib.ptr(ct), ct.numel(), -1,
+                                _lib.stream_of(q))
+        assert rc == 0
+        outs.append((_np(lists), _np(lengths)))
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
