@@ -1270,10 +1270,12 @@ def main() -> int:
     if world > 1:
         import datetime
 
-        # communicator set-up lines (ranks, devices, transports) on stderr; stdout keeps the
-        # one JSON line
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # communicator set-up lines (ranks, devices, transports) on stderr, so a run's log
+        # shows every rank joining; stdout keeps the one JSON line. A bare version request
+        # (NCCL_DEBUG=VERSION, some launchers' default) is raised to the INIT lines.
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
 

@@ -105,8 +105,10 @@ def head_sharded_select(index_queries, positions, bb: BatchedBuckets, config, ga
     [world, ...] (``seqshard.all_gather_fn()`` over NCCL). Returns (lists [B, width],
     lengths [B]) with B = world x this rank's share, in rank order."""
     lists, lengths = batched_select(index_queries, positions, bb, config, top_k)
-    all_lists, all_lengths = gather(lists), gather(lengths)
-    return all_lists.reshape(-1, lists.shape[-1]), all_lengths.reshape(-1)
+    # one exchange: each row's length rides as a last column of its list
+    packed = gather(torch.cat([lists, lengths[:, None]], dim=1))  # [world, share, width + 1]
+    packed = packed.reshape(-1, lists.shape[-1] + 1)
+    return packed[:, :-1], packed[:, -1].contiguous()
 
 
 def shard_rows(B: int, world: int, rank: int) -> tuple[int, int]:
