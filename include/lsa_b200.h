@@ -43,6 +43,15 @@ extern "C" {
 int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, float* iq,
                 float* ik, cudaStream_t stream);
 
+/* regroup through a D-LSA projection map (the reference's "model-specific distilled
+ * projections", docs/ROADMAP.md:41-43, whose upstream map format is absent; this build's
+ * definition): Wt [d_out, Hkv*D] fp32 (16-byte aligned, one row per output dimension);
+ * index query = canonical dots of the group-mean query with Wt's rows, index key = the
+ * concatenated key row's canonical dots with Wt's rows, normalised by their canonical norm.
+ * d and d_out multiples of 8, at most 2048. -> iq / ik [T, d_out] fp32. */
+int lsa_regroup_project(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                        const float* Wt, int64_t d_out, float* iq, float* ik, cudaStream_t stream);
+
 /* F.normalize of each row (pipeline.py:113, :179), optional bf16 copy (round to nearest even). */
 int lsa_normalize_rows(const float* x, int64_t n, int64_t d, float* out, void* out_bf16, cudaStream_t stream);
 

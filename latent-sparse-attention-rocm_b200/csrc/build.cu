@@ -88,6 +88,79 @@ __global__ void __launch_bounds__(kRegroupThreads) regroup_row_kernel(const T* _
     for (int j = tid; j < d; j += kRegroupThreads) ik[t * d + j] = __fdiv_rn(to_f32(row[j]), den);
 }
 
+// regroup through a D-LSA projection map Wt [d_out, d] (fp32, one row per output dim): the
+// group mean of q and the concatenated k row of each position, projected by canonical dots
+// with Wt's rows (lane = chunk mod 32, fmaf chain in chunk order, butterfly), the projected
+// key then normalised by its canonical norm - bit-equal to the checker's regroup_project.
+// A CTA takes 8 positions (staged in shared memory) so each warp's load of a map row serves
+// 8 positions; 8 warps stride the output dims. Dynamic smem: (16 d + 8 d_out) floats.
+constexpr int kProjRows = 8;
+template <typename T, int CH>
+__global__ void __launch_bounds__(256) regroup_project_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                              int64_t Tn, int Hq, int Hkv, int D,
+                                                              const float* __restrict__ Wt, int d_out,
+                                                              float* __restrict__ iq, float* __restrict__ ik) {
+    extern __shared__ __align__(16) float psm[];
+    __shared__ float den_s[kProjRows];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int d = Hkv * D, G = Hq / Hkv;
+    float* xq = psm;                   // [kProjRows][d]
+    float* xk = xq + kProjRows * d;    // [kProjRows][d]
+    float* pk = xk + kProjRows * d;    // [kProjRows][d_out]
+    const int64_t t0 = (int64_t)blockIdx.x * kProjRows;
+    const int rows = (int)(Tn - t0 < kProjRows ? Tn - t0 : kProjRows);
+    for (int i = threadIdx.x; i < rows * d; i += blockDim.x) {
+        const int r = i / d, j = i % d, h = j / D, e = j % D;
+        const int64_t t = t0 + r;
+        float acc = 0.0f;
+        for (int g = 0; g < G; ++g) acc = __fadd_rn(acc, to_f32(q[(t * Hq + h * G + g) * D + e]));
+        xq[r * d + j] = __fdiv_rn(acc, (float)G);
+        xk[r * d + j] = to_f32(k[t * Hkv * D + j]);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int nch = d >> 3;
+    for (int j = warp; j < d_out; j += nw) {
+        float w[CH][8];
+#pragma unroll
+        for (int c = 0; c < CH; ++c) {
+            const int ch = lane + 32 * c;
+            if (ch < nch) load8<float>(Wt + (int64_t)j * d + ch * 8, w[c]);
+        }
+        for (int r = 0; r < rows; ++r) {
+            float pq = 0.0f, pkk = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CH; ++c) {
+                const int ch = lane + 32 * c;
+                if (ch < nch) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        pq = __fmaf_rn(xq[r * d + ch * 8 + e], w[c][e], pq);
+                        pkk = __fmaf_rn(xk[r * d + ch * 8 + e], w[c][e], pkk);
+                    }
+                }
+            }
+            pq = butterfly_sum(pq);
+            pkk = butterfly_sum(pkk);
+            if (lane == 0) {
+                iq[(t0 + r) * d_out + j] = pq;
+                pk[r * d_out + j] = pkk;
+            }
+        }
+    }
+    __syncthreads();
+    if (warp < rows) {
+        const float n = __fsqrt_rn(warp_cdot<float, float>(pk + warp * d_out, pk + warp * d_out, d_out, lane));
+        if (lane == 0) den_s[warp] = fmaxf(n, 1e-12f);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < rows * d_out; i += blockDim.x) {
+        const int r = i / d_out, j = i % d_out;
+        ik[(t0 + r) * d_out + j] = __fdiv_rn(pk[r * d_out + j], den_s[r]);
+    }
+}
+
 // out = x / max(|x|, 1e-12) per row (+ bf16 copy, round to nearest even), one warp per row.
 __global__ void normalize_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ out,
                                  __nv_bfloat16* __restrict__ out_bf16) {
@@ -458,6 +531,49 @@ int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, 
         return LSA_ERR_ARG;
     LSA_LAUNCH_CHECK();
     return LSA_OK;
+}
+
+int lsa_regroup_project(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                        const float* Wt, int64_t d_out, float* iq, float* ik, cudaStream_t stream) {
+    const int64_t d = Hkv * D;
+    if (Hkv <= 0 || Hq % Hkv || D <= 0 || d % 8 || d > 2048 || d_out <= 0 || d_out % 8 || d_out > 2048 ||
+        ((uintptr_t)Wt & 15) || T < 0)
+        return LSA_ERR_ARG;
+    if (T == 0) return LSA_OK;
+    const int smem = (int)((2 * kProjRows * d + kProjRows * d_out) * sizeof(float));
+    cudaLaunchAttribute pdl;
+    pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)((T + kProjRows - 1) / kProjRows));
+    lc.blockDim = dim3(256);
+    lc.dynamicSmemBytes = smem;
+    lc.stream = stream;
+    lc.attrs = &pdl;
+    lc.numAttrs = 1;
+    const int ch = (int)((d / 8 + 31) / 32);
+    auto go = [&](auto kern, auto qp, auto kp) -> int {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return LSA_ERR_CUDA;
+        return cudaLaunchKernelEx(&lc, kern, qp, kp, T, (int)Hq, (int)Hkv, (int)D, Wt, (int)d_out, iq, ik) ==
+                       cudaSuccess
+                   ? LSA_OK
+                   : LSA_ERR_CUDA;
+    };
+#define LSA_RP(TT)                                                                                              \
+    do {                                                                                                        \
+        auto qp = (const TT*)q;                                                                                 \
+        auto kp = (const TT*)k;                                                                                 \
+        if (ch <= 1) return go(regroup_project_kernel<TT, 1>, qp, kp);                                          \
+        if (ch <= 2) return go(regroup_project_kernel<TT, 2>, qp, kp);                                          \
+        if (ch <= 4) return go(regroup_project_kernel<TT, 4>, qp, kp);                                          \
+        return go(regroup_project_kernel<TT, 8>, qp, kp);                                                       \
+    } while (0)
+    if (dtype == kBF16) LSA_RP(__nv_bfloat16);
+    if (dtype == kF16) LSA_RP(__half);
+    if (dtype == kF32) LSA_RP(float);
+#undef LSA_RP
+    return LSA_ERR_ARG;
 }
 
 int lsa_normalize_rows(const float* x, int64_t n, int64_t d, float* out, void* out_bf16, cudaStream_t stream) {

@@ -48,6 +48,7 @@ SIGNATURES = {
     "lsa_sparse_read": (_INT, [_P, _P, _P, _INT, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _I, _P, _I, _I,
                                _P]),
     "lsa_regroup": (_INT, [_P, _P, _INT, _I, _I, _I, _I, _P, _P, _P]),
+    "lsa_regroup_project": (_INT, [_P, _P, _INT, _I, _I, _I, _I, _P, _I, _P, _P, _P]),
     "lsa_normalize_rows": (_INT, [_P, _I, _I, _P, _P, _P]),
     "lsa_build_buckets_workspace": (_I, [_I, _I, _I, _I]),
     "lsa_build_buckets": (_INT, [_P, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _P]),

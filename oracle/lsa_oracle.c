@@ -109,6 +109,36 @@ void ora_regroup(const float *q, const float *k, i64 T, i64 Hq, i64 Hkv, i64 D, 
     }
 }
 
+/* regroup through a D-LSA projection map (the reference's roadmap item "model-specific distilled
+ * projections", docs/ROADMAP.md:41-43; the upstream map format is absent, this build's
+ * definition): with Wt [d_out, d] (the map, one row per output dimension), index query =
+ * cdot(group mean of q, Wt[j]) per output j, index key = unit(cdot(concatenated k row, Wt[j]))
+ * - the canonical dot throughout, the norm over the projected key. */
+void ora_regroup_project(const float *q, const float *k, i64 T, i64 Hq, i64 Hkv, i64 D, const float *Wt, i64 d_out,
+                         float *iq, float *ik) {
+    i64 G = Hq / Hkv, d = Hkv * D;
+    float *xq = (float *)malloc(sizeof(float) * d);
+    float *pk = (float *)malloc(sizeof(float) * d_out);
+    for (i64 t = 0; t < T; ++t) {
+        for (i64 h = 0; h < Hkv; ++h)
+            for (i64 e = 0; e < D; ++e) {
+                float acc = 0.0f;
+                for (i64 g = 0; g < G; ++g) acc = acc + q[(t * Hq + h * G + g) * D + e];
+                xq[h * D + e] = acc / (float)G;
+            }
+        const float *row = k + t * Hkv * D;
+        for (i64 j = 0; j < d_out; ++j) {
+            iq[t * d_out + j] = ora_cdot(xq, Wt + j * d, d);
+            pk[j] = ora_cdot(row, Wt + j * d, d);
+        }
+        float n = sqrtf(ora_cdot(pk, pk, d_out));
+        float den = fmaxf(n, 1e-12f);
+        for (i64 j = 0; j < d_out; ++j) ik[t * d_out + j] = pk[j] / den;
+    }
+    free(xq);
+    free(pk);
+}
+
 /* F.normalize(x, dim=-1) with the canonical norm. */
 void ora_normalize_rows(const float *x, i64 n, i64 d, float *out) {
     for (i64 r = 0; r < n; ++r) {
