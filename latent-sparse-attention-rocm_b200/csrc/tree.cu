@@ -18,12 +18,19 @@
 // CTA of a row (atomic ticket) keeps the row's best keys - a warp-list top-K when the beam
 // / top_p is at most 128, else a full sort - and writes the next level's carried rows (or
 // the picks).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "topk.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lsa {
 
 constexpr int kTreeMaxLevels = 8;
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 constexpr int kTreeSortCap = 8192;
 
 struct TreeGrowth {
@@ -183,6 +190,152 @@ __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
     }
 }
 
+// ------------------------------------------------------------------ cluster beam (few rows)
+
+// One thread-block cluster per row walks every level in ONE launch (the multi-launch form
+// above pays a launch, a ticket round trip and a global key round trip per level):
+//   * before griddepcontrol.wait the cluster pulls every node level's centroid rows into L2
+//     (the hierarchy is read-only here; prefetches cannot observe stale data);
+//   * per level, every CTA derives the level's candidate count from the row's growth and the
+//     previous level's kept count (the same arithmetic in every CTA), scores its share of the
+//     candidates (one warp per candidate, canonical fp32 cdot, the row's query in registers;
+//     carried ids read from the leader's shared memory through DSMEM) and stores the packed
+//     keys into the leader's shared memory;
+//   * one cluster barrier; the leader keeps the best beam_width (top_p at level 0) by warp-list
+//     top-K and writes the next level's carried children into its shared memory; a second
+//     barrier publishes them. Level 0 writes the picks (and their rebased keys).
+// Same picks as the multi-launch form (same candidates, same keys, same order).
+constexpr int kTreeCThreads = 512;
+constexpr int kTreeCWarps = kTreeCThreads / 32;
+constexpr int kTreeCMaxCand = 4096;
+
+struct TreeClusterArgs {
+    const float* q;
+    int64_t d;
+    const int32_t* positions;
+    int64_t block, bpb, nb, size, rows;
+    int top_level, n_built, beam, top_p;
+    const float* lc[kTreeMaxLevels];    // node level l + 1 centroids [n, d] fp32
+    const int64_t* lk[kTreeMaxLevels];  // node level l + 1 children [n, size]
+    int64_t ln[kTreeMaxLevels];         // node level l + 1 node counts
+    const float* bc;                    // bucket centroids_f32 [rows, d]
+    int32_t* picks;                     // [R, top_p]
+    int64_t* pick_keys;                 // [R, top_p] or null
+    int64_t col_offset;
+    int cand_cap, carry_cap;
+    int32_t* status;
+};
+
+struct SmemKeys {
+    const int64_t* k;
+    int n;
+    __device__ int64_t operator()(int i) const { return i < n ? k[i] : kEmpty; }
+};
+
+__device__ __forceinline__ void tc_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tc_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+template <int CHUNKS, int KW>
+__global__ void __launch_bounds__(kTreeCThreads) tree_cluster_kernel(const TreeClusterArgs a) {
+    constexpr int K = 32 * KW;
+    extern __shared__ __align__(16) int64_t csm[];
+    int64_t* keys = csm;                                             // [cand_cap]
+    int64_t* lists = keys + a.cand_cap;                              // [kTreeCWarps * K]
+    int64_t* best = lists + kTreeCWarps * K;                         // [K]
+    int32_t* carried = reinterpret_cast<int32_t*>(best + K);         // [carry_cap]
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank(), cs = (int)cluster.num_blocks();
+    const int r = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // every CTA has started before any DSMEM store (waited on before the first one)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    {
+        const int lines = (int)(a.d * 4 / 128);
+        for (int l = 0; l < a.n_built; ++l)
+            for (int64_t n = (int64_t)rank * kTreeCWarps + warp; n < a.ln[l]; n += (int64_t)cs * kTreeCWarps)
+                for (int i = lane; i < lines; i += 32)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.lc[l] + n * a.d) +
+                                                                  i * 128));
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int64_t pos = a.positions[r];
+    const int64_t page = pos / a.block;
+    TreeGrowth g;
+    growth_at(page, a.bpb, a.nb, a.size, a.top_level, a.rows, a.n_built, g);
+    const int nchunks = (int)(a.d >> 3);
+    float x[CHUNKS][8];
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int ch = min(lane + 32 * j, nchunks - 1);
+        load8<float>(a.q + r * a.d + (size_t)ch * 8, x[j]);
+    }
+    int64_t* lead_keys = cluster.map_shared_rank(keys, 0);
+    const int32_t* lead_carried = cluster.map_shared_rank(carried, 0);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // (first phase)
+    int carried_n = 0;
+    for (int L = a.n_built; L >= 0; --L) {
+        const bool active = L == 0 || g.levels >= L;  // the same in every CTA of the row
+        if (!active) {
+            carried_n = 0;
+            continue;
+        }
+        int n_carried, fresh0, fresh1;
+        if (L == 0) {
+            n_carried = g.levels > 0 ? carried_n : 0;
+            const int64_t vis = page * a.bpb;
+            fresh0 = g.levels > 0 ? g.covered : 0;
+            fresh1 = (int)(vis < a.rows ? vis : a.rows);
+        } else {
+            n_carried = g.levels > L ? carried_n : 0;
+            fresh0 = g.levels == L ? 0 : g.closed[L - 1];
+            fresh1 = g.made[L - 1];
+        }
+        if (fresh1 < fresh0) fresh1 = fresh0;
+        int n_cand = n_carried + (fresh1 - fresh0);
+        if (n_cand > a.cand_cap) {  // never for a consistent hierarchy; recorded, then clamped
+            if (threadIdx.x == 0 && rank == 0) atomicExch(a.status, LSA_ERR_ARG);
+            n_cand = a.cand_cap;
+        }
+        const float* cent = L > 0 ? a.lc[L - 1] : a.bc;
+        for (int i = rank * kTreeCWarps + warp; i < n_cand; i += cs * kTreeCWarps) {
+            const int id = i < n_carried ? lead_carried[i] : fresh0 + (i - n_carried);
+            const float s = butterfly_sum(lane_partial_regs<float, CHUNKS>(x, cent + (int64_t)id * a.d, lane, nchunks));
+            if (lane == 0) lead_keys[i] = pack_key(s, id);
+        }
+        tc_arrive();
+        const int keep = L > 0 ? a.beam : a.top_p;
+        const int kept = n_cand < keep ? n_cand : keep;
+        if (L == 0 && rank != 0) return;  // nothing of this CTA is read after the last scores
+        tc_wait();
+        if (rank == 0) {
+            group_topk_desc<KW, kTreeCWarps>(SmemKeys{keys, n_cand}, n_cand, lists, best, warp, lane,
+                                             TreeBlockSync{});
+            if (L == 0) {
+                for (int i = threadIdx.x; i < a.top_p; i += kTreeCThreads) {
+                    a.picks[(int64_t)r * a.top_p + i] = i < kept ? key_bucket(best[i]) : -1;
+                    if (a.pick_keys) {  // same score bits, column rebased (e.g. to a global bucket id)
+                        int64_t key = kEmpty;
+                        if (i < kept) {
+                            const uint64_t hi = (uint64_t)best[i] & 0xFFFFFFFF00000000ull;
+                            key = (int64_t)(hi |
+                                            (uint32_t)(0x7FFFFFFF - (key_bucket(best[i]) + (int32_t)a.col_offset)));
+                        }
+                        a.pick_keys[(int64_t)r * a.top_p + i] = key;
+                    }
+                }
+                return;
+            }
+            const int S = (int)a.size;
+            for (int i = threadIdx.x; i < kept * S; i += kTreeCThreads)
+                carried[i] = (int32_t)a.lk[L - 1][(int64_t)key_bucket(best[i / S]) * S + (i % S)];
+        }
+        carried_n = kept * (int)a.size;
+        // the leader's carried list (and its finished reads of the keys) before the next scores
+        tc_arrive();
+        tc_wait();
+    }
+}
+
 static int64_t r256(int64_t x) { return (x + 255) / 256 * 256; }
 
 struct TreePlan {
@@ -274,6 +427,59 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
     a.pick_keys = pick_keys;
     a.col_offset = col_offset;
     int chunks = (int)((d / 8 + 31) / 32);
+    // few rows: the whole beam in one cluster launch per row
+    const int ckw = (beam <= 32 && top_p <= 32) ? 1 : ((beam <= 64 && top_p <= 64) ? 2 : ((beam <= 128 && top_p <= 128) ? 4 : 0));
+    if (R <= 64 && ckw && p.cand_cap <= kTreeCMaxCand && size <= 64 && chunks <= 8) {
+        TreeClusterArgs c;
+        c.q = q; c.d = d; c.positions = positions; c.block = block; c.bpb = bpb; c.nb = nb; c.size = size;
+        c.rows = rows; c.top_level = (int)top_level; c.n_built = (int)n_built; c.beam = (int)beam;
+        c.top_p = (int)top_p;
+        for (int l = 0; l < kTreeMaxLevels; ++l) {
+            c.lc[l] = l < n_built ? level_centroids[l] : nullptr;
+            c.lk[l] = l < n_built ? level_children[l] : nullptr;
+            c.ln[l] = l < n_built ? level_counts[l] : 0;
+        }
+        c.bc = bucket_centroids; c.picks = picks; c.pick_keys = pick_keys; c.col_offset = col_offset;
+        c.cand_cap = p.cand_cap; c.carry_cap = p.carry_cap; c.status = counters + R;
+        const int Kc = 32 * ckw;
+        const int csmem = (int)(p.cand_cap * 8 + (kTreeCWarps + 1) * Kc * 8 + ((p.carry_cap + 3) / 4) * 16);
+        int most = p.cand_cap;  // scoring warps the widest level can use
+        int cs = (most + kTreeCWarps * 2 - 1) / (kTreeCWarps * 2);
+        if (cs < 1) cs = 1;
+        if (cs > 16) cs = 16;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        at[1].id = cudaLaunchAttributeClusterDimension;
+        at[1].val.clusterDim.x = (unsigned)cs;
+        at[1].val.clusterDim.y = 1;
+        at[1].val.clusterDim.z = 1;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3((unsigned)cs, (unsigned)R);
+        lc.blockDim = dim3(kTreeCThreads);
+        lc.dynamicSmemBytes = csmem;
+        lc.stream = stream;
+        lc.attrs = at;
+        lc.numAttrs = 2;
+        auto go = [&](auto kern) -> int {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, csmem) != cudaSuccess)
+                return LSA_ERR_CUDA;
+            if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+                return LSA_ERR_CUDA;
+            return cudaLaunchKernelEx(&lc, kern, c) == cudaSuccess ? LSA_OK : LSA_ERR_CUDA;
+        };
+#define LSA_TC_KW(CH)                                               \
+    do {                                                            \
+        if (ckw == 1) return go(tree_cluster_kernel<CH, 1>);        \
+        if (ckw == 2) return go(tree_cluster_kernel<CH, 2>);        \
+        return go(tree_cluster_kernel<CH, 4>);                      \
+    } while (0)
+        if (chunks <= 1) LSA_TC_KW(1);
+        if (chunks <= 2) LSA_TC_KW(2);
+        if (chunks <= 4) LSA_TC_KW(4);
+        LSA_TC_KW(8);
+#undef LSA_TC_KW
+    }
     int smem = next_pow2(p.cand_cap) * 8;
     if (smem < 1024) smem = 1024;
     int sms = 148;
