@@ -51,6 +51,36 @@ def _compile(src: pathlib.Path) -> pathlib.Path:
     return obj
 
 
+TORCH_OPS_SRC = CSRC / "torch_ops.cpp"
+TORCH_OPS_LIB = OUT_DIR / "_lsa_torch_ops.so"
+
+
+def build_torch_ops(force: bool = False) -> pathlib.Path:
+    """The torch.library operators (csrc/torch_ops.cpp): a C++ shared library over the C ABI,
+    compiled against this torch's headers and ABI and linked to liblsa_b200.so beside it."""
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    header = HERE.parent / "include" / "lsa_b200.h"
+    deps = [TORCH_OPS_SRC, header, LIB]
+    if not force and TORCH_OPS_LIB.exists() and all(d.stat().st_mtime <= TORCH_OPS_LIB.stat().st_mtime for d in deps):
+        return TORCH_OPS_LIB
+    cxx = shutil.which("g++") or "g++"
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    torch_lib = pathlib.Path(torch.__file__).resolve().parent / "lib"
+    cuda_home = pathlib.Path(ce.CUDA_HOME or "/usr/local/cuda")
+    incs = [p for p in (ce.include_paths() + [str(cuda_home / "include")])]
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           *[f"-I{i}" for i in incs], str(TORCH_OPS_SRC), "-o", str(TORCH_OPS_LIB) + ".tmp",
+           f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda",
+           f"-L{OUT_DIR}", "-llsa_b200", f"-L{cuda_home / 'lib64'}", "-lcudart", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"torch ops build failed:\n{res.stderr[-4000:]}")
+    os.replace(str(TORCH_OPS_LIB) + ".tmp", TORCH_OPS_LIB)
+    return TORCH_OPS_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
     """Compile every kernel source (in parallel) and link ``liblsa_b200.so`` in place."""
     OBJ_DIR.mkdir(exist_ok=True)
@@ -67,8 +97,9 @@ def build(force: bool = False, verbose: bool = False) -> pathlib.Path:
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr[-4000:]}")
         os.replace(tmp, LIB)
+    build_torch_ops(force)
     if verbose:
-        print(f"built {LIB}")
+        print(f"built {LIB} and {TORCH_OPS_LIB.name}")
     return LIB
 
 

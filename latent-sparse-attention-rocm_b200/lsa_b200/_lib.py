@@ -24,7 +24,7 @@ DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 OK, ERR_ARG, ERR_CUDA, ERR_TIMEOUT, ERR_SHORT, ERR_SIZE = 0, -1, -2, -3, -4, -5
 
 _lib = None
-_lock = threading.Lock()
+_lock = threading.RLock()  # re-entrant: torch_ops() loads lib() first
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int64
@@ -99,6 +99,27 @@ def lib():
                     fn.argtypes = args
                 _lib = handle
     return _lib
+
+
+TORCH_OPS_PATH = pathlib.Path(__file__).resolve().parent / "_lsa_torch_ops.so"
+_torch_ops_loaded = False
+
+
+def torch_ops():
+    """``torch.ops.lsa`` - the hot-path operators registered by ``_lsa_torch_ops.so`` (a C++
+    torch.library over this C ABI, launching on at::cuda::getCurrentCUDAStream()). Raises when
+    the library is missing: there is no fallback."""
+    global _torch_ops_loaded
+    if not _torch_ops_loaded:
+        lib()  # the C-ABI library first (the ops library links against it), outside this lock
+        with _lock:
+            if not _torch_ops_loaded:
+                if not TORCH_OPS_PATH.exists():
+                    raise RuntimeError(f"{TORCH_OPS_PATH} is missing: build it with "
+                                       "latent-sparse-attention-rocm_b200/build.py (needs liblsa_b200.so)")
+                torch.ops.load_library(str(TORCH_OPS_PATH))
+                _torch_ops_loaded = True
+    return torch.ops.lsa
 
 
 def exported_symbols() -> list[str]:
@@ -201,7 +222,10 @@ def check_status(device=None, what: str = "lsa") -> None:
     starts clean, and raises RuntimeError (timeout when a -3 word was found). Graph users
     call it after replays; with LSA_CHECK_STATUS=1 every entry point calls it after its
     launch (outside stream capture)."""
-    bufs = [b for b in list(_ws.counters.values()) + list(_ws.status.values()) if _on(b, device)]
+    cached = list(_ws.counters.values()) + list(_ws.status.values())
+    if _torch_ops_loaded:  # the torch ops' own per-stream counters
+        cached += list(torch.ops.lsa.workspace_counters())
+    bufs = [b for b in cached if _on(b, device)]
     for d in {b.device for b in bufs if b.device.type == "cuda"}:
         torch.cuda.synchronize(d)
     timed_out, dirty = False, False

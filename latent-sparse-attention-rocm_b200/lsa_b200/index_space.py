@@ -24,13 +24,7 @@ def regroup_rows(q: torch.Tensor, k: torch.Tensor):
     Hkv = k.shape[1]
     if Hq % Hkv:
         raise ValueError("query heads must group evenly onto KV heads")
-    q, k = q.contiguous(), k.contiguous()
-    iq = torch.empty(T, Hkv * D, dtype=torch.float32, device=q.device)
-    ik = torch.empty(T, Hkv * D, dtype=torch.float32, device=q.device)
-    if T:
-        check(lib().lsa_regroup(ptr(q), ptr(k), _lib.DTYPE_CODE[q.dtype], T, Hq, Hkv, D, ptr(iq), ptr(ik),
-                                stream_of(q)), "make_index_space")
-    return iq, ik
+    return _lib.torch_ops().regroup(q, k)  # lsa_regroup on the current stream
 
 
 def regroup_project_rows(q: torch.Tensor, k: torch.Tensor, projection: torch.Tensor):

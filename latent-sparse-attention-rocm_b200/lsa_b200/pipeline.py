@@ -368,26 +368,13 @@ def _select_fused(index_queries, positions, buckets, config, top_k, score_dtype)
         raise ValueError(
             f"a position a query: {index_queries.shape[0]} queries, {positions.shape[0]} positions"
         )
-    q, q_code, c = _scoring_operands(index_queries, buckets.centroids, buckets.centroids_f32, score_dtype)
-    R, d = q.shape
-    N = c.shape[0]
-    dev = q.device
-    width = top_k + config.window_size + config.sink_size
-    lists = torch.empty(R, width, dtype=torch.int32, device=dev)
-    lengths = torch.empty(R, dtype=torch.int32, device=dev)
-    if R == 0:
-        return lists, lengths
-    pos = positions.to(torch.int32).contiguous()
-    L = lib()
-    nbytes = L.lsa_select_fused_scratch(R, N)
-    sc = _lib.scratch(nbytes, dev)
-    ct = _lib.counters(R + 1, dev)  # tickets + the status word
-    check(L.lsa_select_fused(ptr(q), q_code, R, d, ptr(c.contiguous()), _lib.DTYPE_CODE[c.dtype],
-                             N, d, ptr(pos), config.cluster_block_size, config.block_bucket_count,
-                             ptr(buckets.members), buckets.members.shape[1], config.top_p, config.window_size,
-                             config.sink_size, top_k, ptr(lists), ptr(lengths), ptr(sc), sc.numel(), ptr(ct),
-                             ct.numel(), -1, stream_of(q)), "flat_select(fused)")
-    _lib.after_call(dev, "flat_select(fused)")
+    c = buckets.centroids_f32 if score_dtype == "fp32" else buckets.centroids
+    # lsa_select_fused through the torch op (current stream; fp32 queries on bf16 centroids are
+    # rounded in-kernel - query code 3)
+    lists, lengths = _lib.torch_ops().select_fused(index_queries, positions, c, buckets.members,
+                                                   config.cluster_block_size, config.block_bucket_count, config.top_p,
+                                                   config.window_size, config.sink_size, top_k)
+    _lib.after_call(index_queries.device, "flat_select(fused)")
     return lists, lengths
 
 

@@ -3,9 +3,10 @@
 Reference: AIwork4me/latent-sparse-attention-rocm, ``src/lsa_rocm_lab/port/read_kernel_tiled.py``
 (numerics ``:41-89``, wrapper ``:92-136``, dispatch ``:144-156``).
 
-One B200 kernel (``lsa_sparse_read``: split-K flash decoding with TMA bulk row gathers)
-serves every launch shape, so ``tile_rows``, ``chunk`` and ``num_warps`` - the reference's
-Triton tunables - are accepted and have no effect. Same contract: q [B, Tq, Hq, Dh],
+One B200 entry point (``lsa_sparse_read``, registered as the torch op ``lsa::sparse_read``)
+serves every launch shape, picking its kernel by the shape (decode rows: one cluster per row
+and KV head; batches: the persistent read; the rest: split-K), so ``tile_rows``, ``chunk`` and
+``num_warps`` - the reference's Triton tunables - are accepted and have no effect. Same contract: q [B, Tq, Hq, Dh],
 k/v [B, Tk, Hkv, Dh], read_ids [B, Tq, width] int32 (-1 padded), lengths [B, Tq];
 lengths are clamped to the width; rows with no listed key read as zeros; duplicates
 count per occurrence; the output has q's shape, dtype and device. Ids outside [0, Tk)
@@ -29,6 +30,11 @@ def _read(q, k, v, read_ids, lengths, scale, splits: int = 0):
     assert Hq % Hkv == 0, "query heads must group evenly onto KV heads"
     if q.dtype not in _lib.DTYPE_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
         raise ValueError(f"q, k, v must share one of fp32/fp16/bf16, got {q.dtype}/{k.dtype}/{v.dtype}")
+    if splits == 0:  # lsa_sparse_read through the torch op, on the current stream
+        out = _lib.torch_ops().sparse_read(q, k, v, read_ids, lengths, D ** -0.5 if scale is None else float(scale))
+        _lib.after_call(q.device, "sparse_read")
+        return out
+    # a forced split count (tests of the split plans): the C ABI directly
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     width = read_ids.shape[-1]
     ids = read_ids.reshape(-1, width).to(torch.int32).contiguous()

@@ -98,3 +98,37 @@ def test_dense_baseline_semantics_on_cpu():
     assert torch.allclose(lsa_b200.dense_read(q[:, -7:], k, v, 0.125), pre[:, -7:], atol=1e-5)
     with pytest.raises(ValueError):
         lsa_b200.dense_read(q, k[:, :32], v[:, :32], 0.125)
+
+
+def test_torch_ops_register_with_shapes():
+    """The torch.library operators (lsa_b200/_lsa_torch_ops.so, over this C ABI) load on a
+    machine without a GPU and give FX / torch.compile their output shapes (Meta kernels)."""
+    import torch
+
+    from lsa_b200 import _lib
+
+    ops = _lib.torch_ops()
+    m = dict(device="meta")
+    q = torch.empty(2, 3, 32, 128, dtype=torch.bfloat16, **m)
+    k = torch.empty(2, 4096, 8, 128, dtype=torch.bfloat16, **m)
+    out = ops.sparse_read(q, k, k, torch.empty(2, 3, 2116, dtype=torch.int32, **m),
+                          torch.empty(2, 3, dtype=torch.int32, **m), 0.1)
+    assert out.shape == q.shape and out.dtype == q.dtype
+    lists, lengths = ops.select_fused(torch.empty(5, 1024, **m), torch.empty(5, dtype=torch.int32, **m),
+                                      torch.empty(512, 1024, dtype=torch.bfloat16, **m),
+                                      torch.empty(512, 128, dtype=torch.int32, **m), 512, 8, 32, 64, 4, 2048)
+    assert lists.shape == (5, 2116) and lengths.shape == (5,) and lists.dtype == torch.int32
+    iq, ik = ops.regroup(torch.empty(7, 32, 128, **m), torch.empty(7, 8, 128, **m))
+    assert iq.shape == ik.shape == (7, 1024) and iq.dtype == torch.float32
+
+
+def test_torch_ops_load_first_in_a_fresh_process():
+    """Loading the torch ops before anything else loads the C-ABI library (a fresh
+    interpreter) returns: the ops loader takes the library first, under a re-entrant lock."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, %r); from lsa_b200 import _lib; "
+            "print(_lib.torch_ops().sparse_read)" % str(ROOT / "latent-sparse-attention-rocm_b200"))
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and "lsa.sparse_read" in res.stdout, res.stderr[-2000:]
