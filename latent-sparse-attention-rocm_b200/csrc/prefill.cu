@@ -110,6 +110,32 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, __half*) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Packed fp32 pairs (sm_100): one instruction does the two lanes' fma / add with the
+// rounding of the scalar instruction; a 3-input max.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // Byte offset of 16-byte chunk c (0..15) of row r in a 128B-swizzled 128 x 128 tile.
 __device__ __forceinline__ uint32_t swz(int r, int c) {
     return (uint32_t)((c >> 3) * kBlockBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
@@ -160,13 +186,16 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bar
                 if (!live) sr[c] = 0xFF800000u;  // -inf
             }
         }
-        float mx8[8];
+        // row max by 3-input max (4 independent chains over the 128 columns)
+        float mx4[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
+        for (int i = 0; i < 4; ++i) mx4[i] = fmaxf(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]));
 #pragma unroll
-        for (int c = 8; c < 128; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], __uint_as_float(sr[c]));
-        const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        for (int c = 8; c < 128; c += 8)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                mx4[i] = max3f(mx4[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+        const float mx = max3f(mx4[0], mx4[1], fmaxf(mx4[2], mx4[3]));
         const float m_new = fmaxf(m_used, mx);
         float alpha = 1.0f;
         const bool resc = m_new > m_used + thresh;
@@ -175,24 +204,31 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bar
             m_used = m_new;
         }
         const float neg = m_used == -INFINITY ? 0.0f : -m_used * sl;
-        float sum8[8];
+        // exponents two columns at a time: one packed FMA (fma.rn.f32x2, the same rounding as
+        // two fmaf) forms (s sl - m sl) for a column pair, one packed add accumulates the pair
+        const uint64_t sl2 = f2_pack(sl, sl), neg2 = f2_pack(neg, neg);
+        uint64_t sum2[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum8[i] = 0.0f;
+        for (int i = 0; i < 4; ++i) sum2[i] = 0ull;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {  // P columns [32 half, 32 half + 32) = keys 64 half ..
             uint32_t pk[32];
 #pragma unroll
             for (int c2 = 0; c2 < 32; ++c2) {
                 const int c = 64 * half + 2 * c2;
-                const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c]), sl, neg));
-                const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c + 1]), sl, neg));
-                sum8[c & 7] += p0;
-                sum8[(c + 1) & 7] += p1;
+                float x0, x1;
+                f2_unpack(ffma2(f2_pack(__uint_as_float(sr[c]), __uint_as_float(sr[c + 1])), sl2, neg2), x0, x1);
+                const float p0 = ex2_approx(x0);
+                const float p1 = ex2_approx(x1);
+                sum2[c2 & 3] = fadd2(sum2[c2 & 3], f2_pack(p0, p1));
                 pk[c2] = pack2(p0, p1, (T*)nullptr);
             }
             tmem_st32(tS + 32 * half, pk);  // P_h over S_h's first 64 columns
         }
-        l = l * alpha + (((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7])));
+        float sm8[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f2_unpack(sum2[i], sm8[2 * i], sm8[2 * i + 1]);
+        l = l * alpha + (((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7])));
         // O_h is current here: PV_h(j-1) was issued before S_h(j) and tcgen05 runs in order
         if (j > 0 && __any_sync(0xFFFFFFFFu, resc)) {
 #pragma unroll

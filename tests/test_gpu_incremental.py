@@ -60,3 +60,44 @@ def test_incremental_index_equals_rebuild(lsa, node_size):
     a = lsa.tree_select(iq, pos, state.buckets, state.hierarchy, cfg)
     b = lsa.tree_select(iq, pos, full_b, full_h, cfg)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy().view(np.uint32)
+
+
+def test_incremental_index_equals_oracle(lsa, oracle):
+    """The maintained index against the CPU checker's full build (oracle.build_buckets +
+    oracle.build_hierarchy over every key so far), bit for bit, at several checkpoints."""
+    from lsa_b200.incremental import IndexState
+    from lsa_b200.index_space import index_keys
+    from lsa_b200.synthetic import drift_keys
+
+    cfg = dict(cluster_block_size=256, pool_size=4, bucket_size=32, bucket_cap=64, top_p=8, top_k=512,
+               window_size=64, sink_size=4, node_bucket_size=4, node_cluster_block_size=32, top_level=2)
+    T = 9000
+    g = torch.Generator(device=DEV)
+    g.manual_seed(7)
+    keys = index_keys(drift_keys(T, 2, 32, g, DEV)[0].to(torch.bfloat16))
+    state = IndexState(keys.shape[1], lsa.PortConfig(**cfg), DEV)
+    ocfg = oracle.Config(**cfg)
+    at = 0
+    for n in (1, 300, 211, 1024, 2000, 5, 2459, 3000):
+        n = min(n, T - at)
+        state.append(keys[at:at + n])
+        at += n
+        if at < cfg["cluster_block_size"]:
+            continue
+        ob = oracle.build_buckets(keys[:at].float().cpu().numpy(), ocfg)
+        b = state.buckets
+        assert (b.members.cpu().numpy() == ob.members).all() and (b.sizes.cpu().numpy() == ob.sizes).all()
+        assert (_bits(b.centroids_f32) == ob.centroids_f32.view(np.uint32)).all()
+        assert (_bits(b.centroids) == ob.centroids_bf16.astype(np.float32).view(np.uint32)).all()
+        assert (_bits(b.key_sums) == ob.key_sums.view(np.uint32)).all()
+        oh = oracle.build_hierarchy(ob, ocfg)
+        assert len(state.hierarchy.levels) == len(oh.levels)
+        for lv, ol in zip(state.hierarchy.levels, oh.levels):
+            assert (lv.children.cpu().numpy() == ol.children).all()
+            assert (_bits(lv.centroids) == ol.centroids.view(np.uint32)).all()
+            assert (_bits(lv.key_sums) == ol.key_sums.view(np.uint32)).all()
+    assert at == T and len(state.hierarchy.levels) >= 1

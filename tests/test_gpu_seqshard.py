@@ -120,3 +120,38 @@ def test_batched_step_equals_per_sequence(lsa, oracle):
     assert got.shape == (3,) + tuple(seqs[0][0].shape[1:])
     for b in range(3):  # one batched read against three single-row reads: same lists, same keys
         assert float((got[b].float() - want[b][0].float()).abs().max()) <= 2e-2
+
+
+def test_batched_step_in_cuda_graph(lsa, oracle):
+    """The batched step captured in a CUDA graph (side-stream fork / join, graph-pool outputs,
+    per-stream scratch sized in the eager warm-up) replays to the eager step's output, byte
+    for byte, and replays again after the inputs change in place."""
+    from lsa_b200 import seqshard
+
+    C = 16384
+    seqs = [_setup(lsa, oracle, C, 1, seed=s) for s in (31, 32)]
+    pos = torch.tensor([C - 1], dtype=torch.int32, device=DEV)
+    gather = lambda x: x[None]
+    pcfg = seqs[0][4]
+    q = torch.cat([s[0] for s in seqs])
+    k = torch.cat([s[1] for s in seqs])
+    v = torch.cat([s[2] for s in seqs])
+    iqs = [s[3] for s in seqs]
+    shards = [s[6][0] for s in seqs]
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        step = lambda: seqshard.seqshard_decode_batch(q, k, v, iqs, pos, shards, pcfg, gather)
+        eager = step().clone()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            out = step()
+        g.replay()
+        stream.synchronize()
+        assert torch.equal(out, eager)
+        q.mul_(0.5)  # new queries in place: the replay must follow them
+        eager2 = step().clone()
+        g.replay()
+        stream.synchronize()
+        assert torch.equal(out, eager2) and not torch.equal(eager2, eager)
+    del g
