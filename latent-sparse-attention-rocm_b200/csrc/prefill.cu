@@ -18,16 +18,20 @@
 //                      written back over S in TMEM (two 16-bit values per column)
 //   O_h += P_h V       tcgen05.mma with A = P from TMEM and V as an MN-major smem operand
 // TMEM columns: S_0/P_0 [0,128), S_1/P_1 [128,256), O_0 [256,384), O_1 [384,512).
-// Rows reach shared memory by cp.async from seven loader warps (16 B per copy into the
+// Rows reach shared memory by cp.async from six loader warps (16 B per copy into the
 // 128B-swizzled layout): Q once, K and V per chunk into 3 + 2 stages. Many small copies in
 // flight beat TMA row gathers here: a tile::gather4 moves 512 B and the copy engine takes
 // roughly 75 cycles per gather, about 7 B/clk per SM.
-// The MMA issue order S_0(j) S_1(j) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ... keeps one half's
-// MMAs running while the other half's softmax works; tcgen05 operations of one thread run
-// in order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and O_h is current
-// whenever the softmax sees S_h(j+1).
-// Warp roles (16 warps): warp 0 issues the MMAs (one thread) and owns the TMEM allocation;
-// warps 1-3 and 12-15 load Q, K and V; warps 4-7 / 8-11 run the softmax of half 0 / half 1.
+// Each half has its own MMA issuing warp: S_h(j), then PV_h(j) in two parts as the half's
+// softmax publishes P_h(j) for the first and the last 64 keys, then S_h(j+1); the tensor pipe interleaves the two halves, so one half's
+// MMAs run while the other half's softmax works. tcgen05 operations of one thread run in
+// order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and O_h is current
+// whenever the softmax sees S_h(j+1). Two issuers because one thread issues one MMA per
+// ~180 cycles (measured on B200: 128 x 128 x 16 MMAs from one thread reach half the pipe's
+// rate, from two threads all of it).
+// Warp roles (16 warps): warps 0 / 1 issue half 0's / half 1's MMAs (warp 0 also owns the
+// TMEM allocation); warps 2-3 and 12-15 load Q, K and V; warps 4-7 / 8-11 run the softmax of
+// half 0 / half 1.
 //
 // Every wait is bounded (1 s of %globaltimer, warp-uniform); a wait that expires raises a
 // CTA-wide abort flag, every role leaves its loop, the MMA warp drains its MMAs and the
@@ -40,7 +44,7 @@ namespace lsa {
 namespace {
 
 constexpr int kPfThreads = 512;
-constexpr int kLoaders = 224;  // warps 1-3 and 12-15
+constexpr int kLoaders = 192;  // warps 2-3 and 12-15
 constexpr int kChunk = 128;                // keys per step
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 16-bit operand tile (two 16 KB blocks)
 constexpr int kBlockBytes = 16384;         // one 64-column block of a tile
@@ -58,10 +62,11 @@ enum : int {
     kBarVFull = kBarKEmpty + kKStages,  // kVStages
     kBarVEmpty = kBarVFull + kVStages,  // kVStages
     kBarSFull = kBarVEmpty + kVStages,  // 2 halves
-    kBarPFull = kBarSFull + 2,          // 2
-    kBarODone = kBarPFull + 2,
-    kBarDrain = kBarODone + 1,
-    kNumBars = kBarDrain + 1
+    kBarPFull = kBarSFull + 2,          // 4: (half, first / last 64 keys of P)
+    kBarODone = kBarPFull + 4,          // 2 halves
+    kBarDrain = kBarODone + 2,          // 2 issuers
+    kBarTurn = kBarDrain + 2,           // 2: half h may run its exponentials
+    kNumBars = kBarTurn + 2
 };
 
 constexpr int kOffMisc = kOffBar + kNumBars * 8;  // TMEM base (u32), abort flag (int)
@@ -171,7 +176,10 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bar
             vm[m] = __ballot_sync(0xFFFFFFFFu, idn[m] >= 0);
             idn[m] = key_id((j + 1) * kChunk + lane + 32 * m);
         }
-        ok = warp_wait(&bars[kBarSFull + h], j & 1, abort_flag);
+        // the halves take turns (h0 chunk j, h1 chunk j, h0 chunk j+1, ...): each turn has the
+        // SM's exponential units to itself while the tensor pipe runs the other half's MMAs
+        if (h == 1 || j > 0) ok = warp_wait(&bars[kBarTurn + h], (h == 1 ? j : j - 1) & 1, abort_flag);
+        if (ok) ok = warp_wait(&bars[kBarSFull + h], j & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         uint32_t sr[128];
@@ -223,28 +231,32 @@ __device__ __forceinline__ void softmax_role(const PrefillArgs& a, uint64_t* bar
                 sum2[c2 & 3] = fadd2(sum2[c2 & 3], f2_pack(p0, p1));
                 pk[c2] = pack2(p0, p1, (T*)nullptr);
             }
+            // O_h is current here (PV_h(j-1) was issued before S_h(j) and tcgen05 runs in
+            // order); its rescale lands before any P of this chunk is published, since PV_h(j)
+            // starts on the first 64 keys' P while the last 64 are still being computed
+            if (half == 0 && j > 0 && __any_sync(0xFFFFFFFFu, resc)) {
+#pragma unroll 1
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t o[32];
+                    tmem_ld32_wait(tO + cc * 32, o);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(tO + cc * 32, o);
+                }
+            }
             tmem_st32(tS + 32 * half, pk);  // P_h over S_h's first 64 columns
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars[kBarPFull + 2 * h + half]);  // keys [64 half, 64 half + 64) of P_h
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars[kBarTurn + (1 - h)]);
         float sm8[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) f2_unpack(sum2[i], sm8[2 * i], sm8[2 * i + 1]);
         l = l * alpha + (((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7])));
-        // O_h is current here: PV_h(j-1) was issued before S_h(j) and tcgen05 runs in order
-        if (j > 0 && __any_sync(0xFFFFFFFFu, resc)) {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t o[32];
-                tmem_ld32_wait(tO + cc * 32, o);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                tmem_st32(tO + cc * 32, o);
-            }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bars[kBarPFull + h]);
     }
-    if (ok && nchunks > 0) ok = warp_wait(&bars[kBarODone], 0, abort_flag);
+    if (ok && nchunks > 0) ok = warp_wait(&bars[kBarODone + h], 0, abort_flag);
     T* orow = static_cast<T*>(a.out) + (((int64_t)b * a.T + t) * a.Hq + (int64_t)kvh * a.G + g) * 128;
     if (ok && nchunks > 0) {
         tc_fence_after();
@@ -307,18 +319,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         mbar_init(&bars[kBarQ], kLoaders);
         for (int s = 0; s < kKStages; ++s) {
             mbar_init(&bars[kBarKFull + s], kLoaders);
-            mbar_init(&bars[kBarKEmpty + s], 1);
+            mbar_init(&bars[kBarKEmpty + s], 2);  // a commit from each half's issuer
         }
         for (int s = 0; s < kVStages; ++s) {
             mbar_init(&bars[kBarVFull + s], kLoaders);
-            mbar_init(&bars[kBarVEmpty + s], 1);
+            mbar_init(&bars[kBarVEmpty + s], 2);
         }
         for (int h = 0; h < 2; ++h) {
             mbar_init(&bars[kBarSFull + h], 1);
-            mbar_init(&bars[kBarPFull + h], 128);
+            mbar_init(&bars[kBarPFull + 2 * h], 128);
+            mbar_init(&bars[kBarPFull + 2 * h + 1], 128);
         }
-        mbar_init(&bars[kBarODone], 1);
-        mbar_init(&bars[kBarDrain], 1);
+        for (int h = 0; h < 2; ++h) {
+            mbar_init(&bars[kBarODone + h], 1);
+            mbar_init(&bars[kBarDrain + h], 1);
+            mbar_init(&bars[kBarTurn + h], 4);  // one arrival per warp of the other half
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -328,17 +344,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // register split (launch: 512 threads x 128): the MMA/loader warpgroups (0 and 3) give
-    // up registers, the two softmax warpgroups take them: 256 x 64 + 256 x 192 = 512 x 128
+    // up registers, the two softmax warpgroups take them: 256 x 80 + 256 x 176 = 512 x 128
     if (warp >= 4 && warp < 12) {
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 192;" ::: "memory");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 176;" ::: "memory");
         softmax_role<T>(a, bars, abort_flag, tmem, key_id, t0, bs, Lt, nchunks);
     } else {
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;" ::: "memory");
-        if (warp == 0) {
-            // ------------------------------------------------------------ MMA issue
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 80;" ::: "memory");
+        if (warp < 2) {
+            // ------------------------------------------------------------ MMA issue, warp h: half h
+            // One issuing thread sustains one tcgen05.mma per ~180 cycles (measured on B200), about
+            // half the tensor pipe's rate at N = 128; the two halves' issuers together keep it full.
+            const int h = warp;
             constexpr uint32_t idS = umma_idesc_f16<T>(128, 128, false);
             constexpr uint32_t idPV = umma_idesc_f16<T>(128, 128, true);
-            auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T
+            auto issue_s = [&](int j) {  // S_h(j) = Q_h K_j^T; K_j's stage is free once both halves' S are
                 if (lane == 0) {
                     fence_proxy_async_smem();  // cp.async (generic proxy) data -> MMA (async proxy)
                     const uint32_t qa = sbase + kOffQ + h * kTileBytes;
@@ -350,17 +369,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                     idS, kk > 0);
                     }
                     umma_commit(&bars[kBarSFull + h]);
+                    umma_commit(&bars[kBarKEmpty + j % kKStages]);
                 }
                 __syncwarp();
             };
-            auto issue_pv = [&](int h, int j) {  // O_h += P_h(j) V_j
+            auto issue_pv = [&](int j, int part) {  // O_h += P_h(j) V_j over keys [64 part, 64 part + 64)
                 if (lane == 0) {
                     fence_proxy_async_smem();
                     const uint32_t va = sbase + kOffV + (j % kVStages) * kTileBytes;
 #pragma unroll 1
-                    for (int kk = 0; kk < 8; ++kk)
+                    for (int kk = 4 * part; kk < 4 * part + 4; ++kk)
                         umma_f16_ts(tmem + 256 + h * 128, tmem + h * 128 + kk * 8,
                                     sw128_desc(va + kk * 2048, kBlockBytes, 1024), idPV, (j > 0 || kk > 0));
+                    if (part == 1) umma_commit(&bars[kBarVEmpty + j % kVStages]);
                 }
                 __syncwarp();
             };
@@ -368,47 +389,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (lane == 0) umma_commit(bar);
                 __syncwarp();
             };
+            // per half, in issue order: S_h(j), then PV_h(j) once the softmax has written P_h(j);
+            // S_h(j + 1) overwrites P_h(j) only after PV_h(j) read it (one thread's tcgen05
+            // operations run in order)
             bool ok = warp_wait(&bars[kBarQ], 0, abort_flag);
-            if (ok && nchunks > 0) ok = warp_wait(&bars[kBarKFull], 0, abort_flag);
-            if (ok && nchunks > 0) {
-                tc_fence_after();
-                issue_s(0, 0);
-                issue_s(1, 0);
-                commit_to(&bars[kBarKEmpty]);
-            }
             for (int j = 0; ok && j < nchunks; ++j) {
-                const bool more = j + 1 < nchunks;
+                ok = warp_wait(&bars[kBarKFull + j % kKStages], (j / kKStages) & 1, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_s(j);
                 ok = warp_wait(&bars[kBarVFull + j % kVStages], (j / kVStages) & 1, abort_flag);
-                if (ok) ok = warp_wait(&bars[kBarPFull + 0], j & 1, abort_flag);
+                if (ok) ok = warp_wait(&bars[kBarPFull + 2 * h], j & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                issue_pv(0, j);
-                if (more) {
-                    const int jn = j + 1;
-                    ok = warp_wait(&bars[kBarKFull + jn % kKStages], (jn / kKStages) & 1, abort_flag);
-                    if (!ok) break;
-                    issue_s(0, jn);
-                }
-                ok = warp_wait(&bars[kBarPFull + 1], j & 1, abort_flag);
+                issue_pv(j, 0);
+                ok = warp_wait(&bars[kBarPFull + 2 * h + 1], j & 1, abort_flag);
                 if (!ok) break;
                 tc_fence_after();
-                issue_pv(1, j);
-                commit_to(&bars[kBarVEmpty + j % kVStages]);
-                if (more) {
-                    issue_s(1, j + 1);
-                    commit_to(&bars[kBarKEmpty + (j + 1) % kKStages]);
-                }
+                issue_pv(j, 1);
             }
-            if (ok && nchunks > 0) commit_to(&bars[kBarODone]);
-            // every MMA issued so far completes before the TMEM is released
-            commit_to(&bars[kBarDrain]);
-            mbar_wait_bounded(&bars[kBarDrain], 0);
+            if (ok && nchunks > 0) commit_to(&bars[kBarODone + h]);
+            // every MMA this warp issued completes before the TMEM is released
+            commit_to(&bars[kBarDrain + h]);
+            mbar_wait_bounded(&bars[kBarDrain + h], 0);
             __syncwarp();
         } else {
-            // ------------------------------------------------------------ loads (warps 1-3, 12-15)
-            // 224 threads, 16 B per cp.async, 128B-swizzled destinations: Q once, then K_j and
+            // ------------------------------------------------------------ loads (warps 2-3, 12-15)
+            // 192 threads, 16 B per cp.async, 128B-swizzled destinations: Q once, then K_j and
             // V_j per chunk into their stages (skipped ids zero-fill their rows: masked anyway)
-            const int lt = (warp < 4 ? warp - 1 : warp - 9) * 32 + lane;
+            const int lt = (warp < 4 ? warp - 2 : warp - 10) * 32 + lane;
             const T* qg = static_cast<const T*>(a.q);
             for (int lin = lt; lin < 4096; lin += kLoaders) {  // 256 rows x 16 chunks
                 const int row2 = lin >> 4, c = lin & 15, h = row2 >> 7, r = row2 & 127, g = r / a.QH, qi = r % a.QH;
