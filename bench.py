@@ -314,6 +314,12 @@ def run_b200(args, rank, world, dev):
         for _ in range(args.steps):
             for L in layers:
                 select(L)
+    # the select from the model's raw query (index query built in the kernel): the e2e step's
+    select_q_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(select_q_graph, stream=stream):
+        for _ in range(args.steps):
+            for L in layers:
+                lsa.select_from_queries(L["q"][0], L["pos"], L["buckets"], pcfg)
 
     def timed(g, reps=1):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -360,6 +366,7 @@ def run_b200(args, rank, world, dev):
         ms_total, per_step = timed_steps(graph, args.steps)
     ms_read = timed(read_graph)
     ms_select = timed(select_graph)
+    ms_select_q = timed(select_q_graph)
     ms_split = timed(split_graph)
     ms_fused = timed(fused_graph)
     if world > 1:
@@ -381,11 +388,12 @@ def run_b200(args, rank, world, dev):
         qd = q_host.to(dev, non_blocking=True)
         outs = []
         for i, L in enumerate(layers):
-            iq, _ = regroup_rows(qd[i, 0], k_last[i])
             if args.decode_impl == "split":
-                lists, lengths = lsa.flat_select(iq, L["pos"], L["buckets"], pcfg)
+                # the index query is built inside the select from the model's query
+                lists, lengths = lsa.select_from_queries(qd[i, 0], L["pos"], L["buckets"], pcfg)
                 outs.append(lsa.lsa_read(qd[i], L["k"], L["v"], lists[None], lengths[None], scale))
             else:
+                iq, _ = regroup_rows(qd[i, 0], k_last[i])
                 outs.append(pipeline.decode_fused(qd[i], L["k"], L["v"], iq, L["pos"], L["buckets"], pcfg, scale))
         out_host.copy_(torch.stack(outs), non_blocking=True)
 
@@ -400,8 +408,10 @@ def run_b200(args, rank, world, dev):
             stream.synchronize()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record(stream)
+            torch.cuda.nvtx.range_push("e2e_eager")  # launch lists: ncu --nvtx --nvtx-include e2e_eager/
             for _ in range(args.steps):
                 e2e_step()
+            torch.cuda.nvtx.range_pop()
             ev1.record(stream)
             stream.synchronize()
             e2e_eager_ms = ev0.elapsed_time(ev1) / args.steps
@@ -540,6 +550,7 @@ def run_b200(args, rank, world, dev):
         "us_per_select_read_split": round(ms_split / args.steps / LAYERS * 1e3, 3),
         "us_per_select_read_fused": round(ms_fused / args.steps / LAYERS * 1e3, 3),
         "us_per_select": round(us_select, 3), "us_per_read": round(us_read, 3),
+        "us_per_select_from_queries": round(ms_select_q / args.steps / LAYERS * 1e3, 3),
         "read_roofline": {"kernel": "lsa::decode_read_kernel", "achieved": round(read_gbs, 1), "unit": "GB/s",
                           "frac": round(read_gbs / hbm, 4)},
         "select_roofline": {"kernel": "lsa::select_decode_kernel", "unit": "GB/s",

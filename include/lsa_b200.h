@@ -39,7 +39,8 @@ extern "C" {
 /* ---------------------------------------------------------------- index space */
 
 /* make_index_space -> upstream regroup (src/lsa_rocm_lab/port/gates.py:50-59).
- * q [T, Hq, D], k [T, Hkv, D] (dtype) -> index queries / unit index keys [T, Hkv*D] fp32. */
+ * q [T, Hq, D], k [T, Hkv, D] (dtype) -> index queries / unit index keys [T, Hkv*D] fp32.
+ * k = NULL: index queries only (ik unused). */
 int lsa_regroup(const void* q, const void* k, int dtype, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, float* iq,
                 float* ik, cudaStream_t stream);
 
@@ -135,6 +136,19 @@ int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, c
                      int64_t cap, int64_t top_p, int64_t window, int64_t sink, int64_t top_k, int32_t* lists,
                      int32_t* lengths, void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
                      int64_t max_position, cudaStream_t stream);
+
+/* make_index_space + flat_select (fused) for decode rows in one launch (gates.py:50-59 then
+ * pipeline.py:274-316): q [R, Hq, D] raw queries (q_dtype fp32 / fp16 / bf16); the index
+ * query of a row is built in the kernel with lsa_regroup's arithmetic (the group mean of
+ * each KV head's query heads, read as its bf16 rounding for bf16 centroids), so the lists
+ * equal lsa_regroup followed by lsa_select_fused byte for byte. Rows the one-cluster decode
+ * select takes (R < 256, top_p <= 32, cap <= 128, N <= 1024 columns, Hkv*D <= 2048 in
+ * chunks that fit its registers) only: anything else returns LSA_ERR_ARG and the caller
+ * regroups and calls lsa_select_fused. No scratch, no counters. */
+int lsa_select_fused_grouped(const void* q, int q_dtype, int64_t R, int64_t Hq, int64_t Hkv, int64_t D,
+                             const void* centroids, int c_dtype, int64_t N, const int32_t* positions, int64_t block,
+                             int64_t bpb, const int32_t* members, int64_t cap, int64_t top_p, int64_t window,
+                             int64_t sink, int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream);
 
 /* cfg 2's positional block-sparse arm (pipeline.py:378-403 builds its buckets; the static
  * pattern is this build's definition): per row, of the v visible buckets the first `first`,

@@ -34,6 +34,7 @@ __global__ void regroup_kernel(const T* __restrict__ q, const T* __restrict__ k,
         for (int g = 0; g < G; ++g) acc = __fadd_rn(acc, to_f32(q[(t * Hq + h * G + g) * D + e]));
         iq[t * d + j] = __fdiv_rn(acc, (float)G);
     }
+    if (k == nullptr) return;  // index queries only
     const T* row = k + t * Hkv * D;
     float n = __fsqrt_rn(warp_cdot<T, T>(row, row, d, lane));
     float den = fmaxf(n, 1e-12f);
@@ -68,7 +69,7 @@ __global__ void __launch_bounds__(kRegroupThreads) regroup_row_kernel(const T* _
         for (int g = 0; g < 8; ++g) qv[i][g] = to_f32(q[(t * Hq + h * G + min(g, G - 1)) * D + e]);
     }
     const T* row = k + t * Hkv * D;
-    if (tid < 32) {
+    if (k != nullptr && tid < 32) {
         const float n = __fsqrt_rn(warp_cdot<T, T>(row, row, d, tid));
         if (tid == 0) den_s = fmaxf(n, 1e-12f);
     }
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(kRegroupThreads) regroup_row_kernel(const T* _
             iq[t * d + j] = __fdiv_rn(acc, (float)G);
         }
     }
+    if (k == nullptr) return;  // index queries only (block-uniform)
     __syncthreads();
     const float den = den_s;
     for (int j = tid; j < d; j += kRegroupThreads) ik[t * d + j] = __fdiv_rn(to_f32(row[j]), den);

@@ -54,6 +54,25 @@ template <> __device__ __forceinline__ void load8<F32AsBF16>(const F32AsBF16* p,
     for (int e = 0; e < 8; ++e) out[e] = __bfloat162float(__float2bfloat16_rn(out[e]));
 }
 
+// A query read as its index-space row, built inside the select: the storage is the raw
+// query [R, Hq, D] of T, and index element (h, e) is the fp32 mean of q[h G + g][e] over the
+// G query heads of KV head h (added in head order from 0, then divided by G: the regroup's
+// arithmetic), read as its bf16 rounding when RB (bf16 scoring).
+template <typename T, bool RB> struct GroupMean {
+    T v;
+};
+template <typename T> struct GroupMeanOf {
+    static constexpr bool value = false;
+};
+template <typename T, bool RB> struct GroupMeanOf<GroupMean<T, RB>> {
+    static constexpr bool value = true;
+    static constexpr bool round_bf16 = RB;
+    using raw = T;
+};
+struct QGroup {
+    int G, D;  // query heads per KV head, head dim (GroupMean queries only)
+};
+
 template <> __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&out)[8]) {
     uint4 u = *reinterpret_cast<const uint4*>(p);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};

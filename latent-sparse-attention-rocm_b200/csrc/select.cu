@@ -14,6 +14,8 @@
 //                  (rows wider than one cluster: the last CTA by atomic ticket does it).
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "topk.cuh"
 #include "umma.cuh"
@@ -309,6 +311,7 @@ struct RowPos {
 };
 
 constexpr int kFusedThreads = 512;
+constexpr int kDecodeMaxD = 2048;  // index dims the decode select stages for a built query
 constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
 constexpr int kGatherMax = 8192;       // read-list slots the fused selects gather in shared memory
 
@@ -763,7 +766,7 @@ template <typename TQ, typename TC, int CHUNKS, int CPW>
 __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
     const TQ* __restrict__ q, int64_t ldq, const TC* __restrict__ c, int64_t N, int d, RowPos rp, int64_t block,
     int64_t bpb, int top_p, const int32_t* __restrict__ members, int cap, int window, int sink, int top_k,
-    int32_t* __restrict__ lists, int32_t* __restrict__ lengths) {
+    int32_t* __restrict__ lists, int32_t* __restrict__ lengths, QGroup qg) {
     static_assert(CPW == 1 || CPW == 2 || CPW == 4, "16, 32 or 64 columns per CTA");
     __shared__ int64_t lead[16 * 32];           // the cluster's sorted 32-lists (leader's copy is used)
     __shared__ int64_t local[16 * CPW];         // this CTA's keys, column order
@@ -804,10 +807,12 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
                    // the compiler issues all of them before the first use
         float x[CHUNKS][8];
         RawChunk<TC> raw[CPW][CHUNKS];
+        if constexpr (!GroupMeanOf<TQ>::value) {
 #pragma unroll
-        for (int j = 0; j < CHUNKS; ++j) {
-            const int ch = min(lane + 32 * j, nchunks - 1);
-            load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+            for (int j = 0; j < CHUNKS; ++j) {
+                const int ch = min(lane + 32 * j, nchunks - 1);
+                load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
+            }
         }
 #pragma unroll
         for (int i = 0; i < CPW; ++i) {
@@ -817,6 +822,39 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
             for (int j = 0; j < CHUNKS; ++j) {
                 const int ch = min(lane + 32 * j, nchunks - 1);
                 raw[i][j].load(cr + n * d + (size_t)ch * 8);
+            }
+        }
+        if constexpr (GroupMeanOf<TQ>::value) {
+            // the index query from the raw query row (the centroid loads above are in flight):
+            // thread i builds chunk i (8 elements of one KV head) in shared memory
+            using TR = typename GroupMeanOf<TQ>::raw;
+            __shared__ __align__(16) float qsm[kDecodeMaxD];
+            const TR* qr = reinterpret_cast<const TR*>(q) + r * ldq;
+            for (int i = threadIdx.x; i < nchunks; i += kDecodeSelThreads) {
+                const int j0 = i * 8, h = j0 / qg.D, e0 = j0 - h * qg.D;
+                const TR* base = qr + (int64_t)h * qg.G * qg.D + e0;
+                float acc[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll 4
+                for (int g = 0; g < qg.G; ++g) {
+                    float v[8];
+                    load8<TR>(base + (int64_t)g * qg.D, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float m = __fdiv_rn(acc[e], (float)qg.G);
+                    if (GroupMeanOf<TQ>::round_bf16) m = __bfloat162float(__float2bfloat16_rn(m));
+                    qsm[j0 + e] = m;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < CHUNKS; ++j) {
+                const int ch = min(lane + 32 * j, nchunks - 1);
+                load8<float>(qsm + ch * 8, x[j]);
             }
         }
         float part[CPW];
@@ -1506,7 +1544,7 @@ static int select_fused_launch(const void* queries, int q_dtype, int64_t R, int6
                 return LSA_ERR_CUDA;                                                                             \
             return cudaLaunchKernelEx(&dc, kern, (const TQ*)queries, ldq, (const TC*)centroids, N, (int)d,       \
                                       positions, block, bpb, (int)top_p, members, (int)cap, (int)window,         \
-                                      (int)sink, (int)top_k, lists, lengths) == cudaSuccess                      \
+                                      (int)sink, (int)top_k, lists, lengths, QGroup{0, 0}) == cudaSuccess        \
                        ? LSA_OK                                                                                  \
                        : LSA_ERR_CUDA;                                                                           \
         };                                                                                                       \
@@ -1609,6 +1647,98 @@ int lsa_select_batched(const void* queries, int q_dtype, int64_t R, int64_t ldq,
                                RowPos{positions, 0, block, table_off, table_rows}, block, bpb, members, cap, top_p,
                                window, sink, top_k, lists, lengths, scratch, scratch_bytes, counters, n_counters,
                                max_position, stream);
+}
+
+int lsa_select_fused_grouped(const void* q, int q_dtype, int64_t R, int64_t Hq, int64_t Hkv, int64_t D,
+                             const void* centroids, int c_dtype, int64_t N, const int32_t* positions, int64_t block,
+                             int64_t bpb, const int32_t* members, int64_t cap, int64_t top_p, int64_t window,
+                             int64_t sink, int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
+    // the decode rows select_fused would give to the one-cluster decode kernel, with the
+    // index query built in the kernel; anything else is refused (LSA_ERR_ARG) for the caller
+    // to regroup and call lsa_select_fused
+    if (R < 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv || D <= 0 || D % 8 || positions == nullptr) return LSA_ERR_ARG;
+    const int64_t d = Hkv * D, G = Hq / Hkv;
+    if (d > kDecodeMaxD || cap <= 0 || block <= 0 || top_p <= 0 || top_k < 0 || window < 0 || sink < 0)
+        return LSA_ERR_ARG;
+    if (!aligned16(q) || !aligned16(centroids)) return LSA_ERR_ARG;
+    if (q_dtype != kBF16 && q_dtype != kF16 && q_dtype != kF32) return LSA_ERR_ARG;
+    if (c_dtype != kBF16 && c_dtype != kF32) return LSA_ERR_ARG;
+    const int64_t most = N;
+    int cpw = (int)((most + 16 * 16 - 1) / (16 * 16));
+    if (cpw < 1) cpw = 1;
+    int cs = (int)((most + 16 * cpw - 1) / (16 * cpw));
+    if (cs < 1) cs = 1;
+    const int ch = (int)((d / 8 + 31) / 32);
+    const int dcpw = cpw <= 1 ? 1 : (cpw <= 2 ? 2 : 4);
+    const bool decode = R < 256 && cpw <= kMaxColsPerWarp && cs <= 16 && R * most < 8192 && top_p <= 32 &&
+                        cap <= kDecodeMaxCap && ch * dcpw * (c_dtype == kF32 ? 2 : 1) <= 8;
+    if (!decode) return LSA_ERR_ARG;
+    if (R == 0) return LSA_OK;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    attrs[1].id = cudaLaunchAttributeClusterDimension;
+    const int dcs = (int)((most + kDecodeSelWarps * dcpw - 1) / (kDecodeSelWarps * dcpw));
+    attrs[1].val.clusterDim.x = (unsigned)(dcs < 1 ? 1 : dcs);
+    attrs[1].val.clusterDim.y = 1;
+    attrs[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t dc = {};
+    dc.gridDim = dim3(attrs[1].val.clusterDim.x, (unsigned)R);
+    dc.blockDim = dim3(kDecodeSelThreads);
+    dc.dynamicSmemBytes = 0;
+    dc.stream = stream;
+    dc.attrs = attrs;
+    dc.numAttrs = 2;
+    const RowPos rp{positions, 0, block, nullptr, nullptr};
+    const QGroup qg{(int)G, (int)D};
+    const int64_t ldq = Hq * D;
+    int rc = LSA_ERR_ARG;
+    // only the (chunks per lane, columns per warp) pairs the decode condition admits are built
+    auto run = [&](auto tq, auto tc) -> int {
+        using TQ = decltype(tq);
+        using TC = decltype(tc);
+        constexpr int wide = sizeof(TC) == 4 ? 2 : 1;
+        int out = LSA_ERR_ARG;
+        auto go = [&](auto kern) {
+            if (dcs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+                out = LSA_ERR_CUDA;
+            else
+                out = cudaLaunchKernelEx(&dc, kern, (const TQ*)q, ldq, (const TC*)centroids, N, (int)d, rp, block, bpb,
+                                         (int)top_p, members, (int)cap, (int)window, (int)sink, (int)top_k, lists,
+                                         lengths, qg) == cudaSuccess
+                          ? LSA_OK
+                          : LSA_ERR_CUDA;
+        };
+        auto pick = [&](auto chc) {
+            constexpr int CH = decltype(chc)::value;
+            if constexpr (CH * wide <= 8) {
+                if (dcpw == 1) go(select_decode_kernel<TQ, TC, CH, 1>);
+            }
+            if constexpr (CH * 2 * wide <= 8) {
+                if (dcpw == 2) go(select_decode_kernel<TQ, TC, CH, 2>);
+            }
+            if constexpr (CH * 4 * wide <= 8) {
+                if (dcpw == 4) go(select_decode_kernel<TQ, TC, CH, 4>);
+            }
+        };
+        if (ch <= 1) pick(std::integral_constant<int, 1>{});
+        else if (ch <= 2) pick(std::integral_constant<int, 2>{});
+        else if (ch <= 4) pick(std::integral_constant<int, 4>{});
+        else pick(std::integral_constant<int, 8>{});
+        return out;
+    };
+    if (c_dtype == kBF16) {  // bf16 scoring: the built query read as its bf16 rounding
+        if (q_dtype == kBF16) rc = run(GroupMean<__nv_bfloat16, true>{}, __nv_bfloat16{});
+        else if (q_dtype == kF16) rc = run(GroupMean<__half, true>{}, __nv_bfloat16{});
+        else rc = run(GroupMean<float, true>{}, __nv_bfloat16{});
+    } else {  // fp32 scoring
+        if (q_dtype == kBF16) rc = run(GroupMean<__nv_bfloat16, false>{}, float{});
+        else if (q_dtype == kF16) rc = run(GroupMean<__half, false>{}, float{});
+        else rc = run(GroupMean<float, false>{}, float{});
+    }
+    if (rc != LSA_OK) return rc;
+    LSA_LAUNCH_CHECK();
+    return LSA_OK;
 }
 
 int lsa_select_fused(const void* queries, int q_dtype, int64_t R, int64_t ldq, const void* centroids, int c_dtype,

@@ -6,6 +6,7 @@
 //   lsa::regroup(q, k) -> (index_queries, index_keys)        make_index_space, port/gates.py:50-59
 //   lsa::select_fused(index_queries, positions, centroids, members, block, bpb, top_p, window,
 //                     sink, top_k) -> (lists, lengths)          flat_select fused, pipeline.py:274-316
+//                     (index_queries [R, d], or raw queries [R, Hq, D]: regroup fused in)
 //   lsa::sparse_read(q, k, v, ids, lengths, scale) -> out     sparse_read_auto, read_kernel_tiled.py:147
 //   lsa::workspace_counters() -> Tensor[]                      the cached counter buffers (checks)
 // Meta implementations give FX / torch.compile the output shapes. Workspaces: scratch (any
@@ -77,18 +78,49 @@ std::tuple<at::Tensor, at::Tensor> regroup_cuda(const at::Tensor& q_in, const at
     return {iq, ik};
 }
 
-std::tuple<at::Tensor, at::Tensor> select_fused_cuda(const at::Tensor& iq_in, const at::Tensor& positions_in,
+std::tuple<at::Tensor, at::Tensor> select_fused_cuda(const at::Tensor& iq_arg, const at::Tensor& positions_in,
                                                      const at::Tensor& centroids_in, const at::Tensor& members_in,
                                                      int64_t block, int64_t bpb, int64_t top_p, int64_t window,
                                                      int64_t sink, int64_t top_k) {
-    TORCH_CHECK(iq_in.is_cuda() && positions_in.is_cuda() && centroids_in.is_cuda() && members_in.is_cuda(),
+    TORCH_CHECK(iq_arg.is_cuda() && positions_in.is_cuda() && centroids_in.is_cuda() && members_in.is_cuda(),
                 "lsa::select_fused is a CUDA kernel");
-    TORCH_CHECK(iq_in.dim() == 2 && centroids_in.dim() == 2 && iq_in.size(1) == centroids_in.size(1),
-                "lsa::select_fused: index_queries [R, d], centroids [N, d]");
-    TORCH_CHECK(positions_in.numel() == iq_in.size(0), "lsa::select_fused: a position a query");
-    c10::cuda::CUDAGuard guard(iq_in.device());
+    TORCH_CHECK(centroids_in.dim() == 2, "lsa::select_fused: centroids [N, d]");
+    c10::cuda::CUDAGuard guard(iq_arg.device());
     const auto cdt = centroids_in.scalar_type();
     TORCH_CHECK(cdt == at::kBFloat16 || cdt == at::kFloat, "lsa::select_fused: bf16 or fp32 centroids");
+    at::Tensor iq_in = iq_arg;
+    if (iq_arg.dim() == 3) {
+        // raw queries [R, Hq, D]: the index queries are built inside the decode select (one
+        // launch); rows it does not take are regrouped first and go the two-dimensional way
+        auto qr = iq_arg.contiguous();
+        const int64_t R = qr.size(0), Hq = qr.size(1), D = qr.size(2), d = centroids_in.size(1);
+        TORCH_CHECK(D > 0 && d % D == 0 && Hq % (d / D) == 0,
+                    "lsa::select_fused: raw queries [R, Hq, D] need centroids of Hkv * D dims with Hq % Hkv == 0");
+        TORCH_CHECK(positions_in.numel() == R, "lsa::select_fused: a position a query");
+        const int64_t Hkv = d / D;
+        auto c = centroids_in.contiguous();
+        auto members = members_in.to(at::kInt).contiguous();
+        auto pos = positions_in.to(at::kInt).contiguous();
+        const int64_t width = top_k + window + sink;
+        auto lists = at::empty({R, width}, qr.options().dtype(at::kInt));
+        auto lengths = at::empty({R}, qr.options().dtype(at::kInt));
+        if (R == 0) return {lists, lengths};
+        auto stream = at::cuda::getCurrentCUDAStream();
+        const int rc = lsa_select_fused_grouped(qr.data_ptr(), dtype_code(qr.scalar_type()), R, Hq, Hkv, D,
+                                                c.data_ptr(), cdt == at::kFloat ? 0 : 2, c.size(0),
+                                                pos.data_ptr<int32_t>(), block, bpb, members.data_ptr<int32_t>(),
+                                                members.size(1), top_p, window, sink, top_k,
+                                                lists.data_ptr<int32_t>(), lengths.data_ptr<int32_t>(), stream);
+        if (rc == LSA_OK) return {lists, lengths};
+        TORCH_CHECK(rc == LSA_ERR_ARG, "lsa::select_fused: the C-ABI entry point returned status ", rc);
+        iq_in = at::empty({R, d}, qr.options().dtype(at::kFloat));
+        check_rc(lsa_regroup(qr.data_ptr(), nullptr, dtype_code(qr.scalar_type()), R, Hq, Hkv, D,
+                             iq_in.data_ptr<float>(), nullptr, stream),
+                 "lsa::select_fused");
+    }
+    TORCH_CHECK(iq_in.dim() == 2 && iq_in.size(1) == centroids_in.size(1),
+                "lsa::select_fused: index_queries [R, d] (or raw queries [R, Hq, D]), centroids [N, d]");
+    TORCH_CHECK(positions_in.numel() == iq_in.size(0), "lsa::select_fused: a position a query");
     at::Tensor q;
     int q_code;
     if (cdt == at::kFloat) {  // fp32 scoring

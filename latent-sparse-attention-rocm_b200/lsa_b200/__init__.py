@@ -23,6 +23,7 @@ from .pipeline import (  # noqa: F401
     flat_select_reference,
     lsa_read,
     position_buckets,
+    select_from_queries,
     tree_select,
     visible_counts,
 )
@@ -30,5 +31,6 @@ from .pipeline import (  # noqa: F401
 __all__ = [
     "Buckets", "Hierarchy", "NodeLevel", "PortConfig", "best_first_keys", "build_buckets_gpu",
     "build_hierarchy_gpu", "dense_read", "flat_select", "flat_select_reference", "lsa_read",
-    "make_index_space", "position_buckets", "tree_select", "visible_counts", "check_status",
+    "make_index_space", "position_buckets", "select_from_queries", "tree_select", "visible_counts",
+    "check_status",
 ]

@@ -42,6 +42,8 @@ SIGNATURES = {
     "lsa_expand_in_order": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
     "lsa_expand_from_keys": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
     "lsa_select_fused_scratch": (_I, [_I, _I]),
+    "lsa_select_fused_grouped": (_INT, [_P, _INT, _I, _I, _I, _I, _P, _INT, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I,
+                                        _P, _P, _P]),
     "lsa_select_fused": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P, _P,
                                 _I, _P, _I, _I, _P]),
     "lsa_sparse_read_plan": (_INT, [_I, _I, _I, _I, _I, _I, _I, _P, _P, _P]),

@@ -405,6 +405,31 @@ def flat_select(index_queries, positions, buckets, config, top_k=None, score_dty
                                                   config.sink_size, top_k)
 
 
+def select_from_queries(q, positions, buckets, config, top_k=None, score_dtype="bf16"):
+    """``make_index_space`` + ``flat_select`` (fused) from raw queries, for decode steps.
+
+    q [R, Hq, D] (one row per decoding sequence, Hq a multiple of the index's KV heads):
+    the index query of each row (the group mean of every KV head's query heads) is built
+    inside the decode select kernel, so one launch goes from the model's query to the read
+    lists - the same lists as ``flat_select(regroup_rows(q, ...)[0], ...)`` byte for byte.
+    Rows the one-cluster decode select does not take are regrouped first (on the GPU) and go
+    the fused two-step way. Reference: ``src/lsa_rocm_lab/port/gates.py:50-59`` (the index
+    space) and ``src/lsa_rocm_lab/port/pipeline.py:274-316`` (the fused select).
+    """
+    require_cuda(q, positions, what="select_from_queries")
+    if q.dim() != 3:
+        raise ValueError(f"raw queries are [R, Hq, D], got shape {tuple(q.shape)}")
+    if positions.shape[0] != q.shape[0]:
+        raise ValueError(f"a position a query: {q.shape[0]} queries, {positions.shape[0]} positions")
+    top_k = config.top_k if top_k is None else top_k
+    c = buckets.centroids_f32 if score_dtype == "fp32" else buckets.centroids
+    lists, lengths = _lib.torch_ops().select_fused(q, positions, c, buckets.members, config.cluster_block_size,
+                                                   config.block_bucket_count, config.top_p, config.window_size,
+                                                   config.sink_size, top_k)
+    _lib.after_call(q.device, "select_from_queries")
+    return lists, lengths
+
+
 def tree_select(index_queries, positions, buckets, hierarchy, config, top_k=None):
     """Select each query's keys by a beam down the levels (ref ``pipeline.py:319-337``)."""
     from ._tree import tree_select_batched

@@ -250,3 +250,51 @@ def test_fp32_queries_read_as_bf16_equal_cast_queries(lsa, R, N, top_p, cap, d):
         assert rc == 0
         outs.append((_np(lists), _np(lengths)))
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+
+
+SFQ_CFG = dict(cluster_block_size=512, pool_size=4, bucket_size=64, bucket_cap=128, top_p=32, top_k=2048,
+               window_size=64, sink_size=4)
+
+
+@pytest.mark.parametrize("dtype,Hq,Hkv,D,score_dtype", [
+    ("bf16", 32, 8, 128, "bf16"), ("fp16", 8, 2, 64, "fp32"), ("fp32", 16, 1, 128, "bf16"),
+    ("bf16", 4, 4, 32, "bf16"), ("bf16", 16, 2, 64, "fp32"),
+])
+def test_select_from_queries_equals_regroup_then_select(oracle, lsa, dtype, Hq, Hkv, D, score_dtype):
+    """One launch from the model's raw queries (the index query built inside the decode select)
+    gives the lists of regroup + the fused select, byte for byte, and the checker's lists;
+    the 300-row batch goes the regroup-first way (more rows than the decode select takes)."""
+    from lsa_b200.index_space import regroup_rows
+
+    T = 4096
+    rng = np.random.default_rng(Hq * 100 + D)
+    tdt = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[dtype]
+    q = torch.from_numpy(rng.standard_normal((T, Hq, D)).astype(np.float32)).to(DEV).to(tdt)
+    from conftest import drift_keys
+
+    k = torch.from_numpy(drift_keys(rng, T, Hkv, D)).to(DEV).to(tdt)
+    iq_np, ik_np = oracle.regroup(q.float().cpu().numpy(), k.float().cpu().numpy())
+    ocfg = oracle.Config(**SFQ_CFG)
+    ob = oracle.build_buckets(ik_np, ocfg)
+    b = oracle_buckets_to_gpu(ob)
+    pcfg = lsa.PortConfig(**SFQ_CFG)
+    iq, _ = regroup_rows(q, k)
+    assert (iq.cpu().numpy().view(np.uint32) == iq_np.view(np.uint32)).all()
+    for pos in ([T - 1], [0], [0, 1, 511, 512, 513, 1024, 2047, 3000, T - 1], list(range(T - 300, T))):
+        pos_np = np.array(pos)
+        pt = torch.from_numpy(pos_np).to(DEV)
+        got = lsa.select_from_queries(q[pt], pt, b, pcfg, score_dtype=score_dtype)
+        two = lsa.pipeline._select_fused(iq[pt], pt, b, pcfg, pcfg.top_k, score_dtype)
+        assert torch.equal(got[0], two[0]) and torch.equal(got[1], two[1])
+        want = oracle.flat_select(iq_np[pos_np], pos_np, ob, ocfg, score_dtype=score_dtype)
+        assert (_np(got[0]) == want[0]).all() and (_np(got[1]) == want[1]).all()
+
+
+def test_select_from_queries_rejects_bad_shapes(lsa):
+    b = lsa.Buckets(torch.zeros(4, 64, device=DEV, dtype=torch.bfloat16), torch.zeros(4, 8, device=DEV,
+                    dtype=torch.int32), torch.zeros(4, device=DEV, dtype=torch.int32))
+    pos = torch.tensor([7], device=DEV)
+    with pytest.raises(ValueError, match="raw queries"):
+        lsa.select_from_queries(torch.zeros(1, 64, device=DEV), pos, b, lsa.PortConfig())
+    with pytest.raises(RuntimeError, match="Hkv"):  # 64 index dims do not split into heads of 48
+        lsa.select_from_queries(torch.zeros(1, 4, 48, device=DEV), pos, b, lsa.PortConfig())
