@@ -749,9 +749,13 @@ __global__ void __launch_bounds__(kReadThreads, 2) decode_read_kernel(ReadArgs a
     const T* kbase = reinterpret_cast<const T*>(a.k) + (b * a.Tk * a.Hkv + h) * D;
     const T* vbase = reinterpret_cast<const T*>(a.v) + (b * a.Tk * a.Hkv + h) * D;
     const int64_t tstride = (int64_t)a.Hkv * D;
-    auto issue = [&](int j0, int j1) {
-        for (int i = tid; i < (j1 - j0) * 2 * LPR; i += kReadThreads) {
-            const int j = j0 + i / (2 * LPR), pc = i % (2 * LPR);
+    // every warp copies the K and V rows of exactly the slots it computes on and waits only
+    // for its own copies: a warp starts its tensor pass as soon as its rows have landed
+    const int kb = warp * SPW;  // this warp's slots: one pass over the whole slice
+    {
+        const int nw = max(0, min(SPW, n_here - kb));
+        for (int i = lane; i < nw * 2 * LPR; i += 32) {
+            const int j = kb + i / (2 * LPR), pc = i % (2 * LPR);
             const int idj = sid[j];
             if (idj >= 0) {
                 const bool isv = pc >= LPR;
@@ -761,17 +765,15 @@ __global__ void __launch_bounds__(kReadThreads, 2) decode_read_kernel(ReadArgs a
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    issue(0, n_here);
+    }
 
     float o[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
     float mrow = kNegBig, lrow = 0.0f;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
+    __syncwarp();
     {
-        const int kb = warp * SPW;  // this warp's slots: one pass over the whole slice
         if (kb < n_here) {
             const unsigned char* fl = sflag + kb;
             if (__any_sync(0xFFFFFFFFu, fl[lane % SPW] != 0))
