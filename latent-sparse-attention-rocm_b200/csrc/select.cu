@@ -312,6 +312,13 @@ struct RowPos {
 
 constexpr int kFusedThreads = 512;
 constexpr int kDecodeMaxD = 2048;  // index dims the decode select stages for a built query
+// the raw element type of a built query (GroupMean<T, RB> -> T; other query types: a stand-in)
+template <typename TQ> struct QRawOf {
+    using type = __nv_bfloat16;
+};
+template <typename T, bool RB> struct QRawOf<GroupMean<T, RB>> {
+    using type = T;
+};
 constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
 constexpr int kGatherMax = 8192;       // read-list slots the fused selects gather in shared memory
 
@@ -727,7 +734,7 @@ constexpr int kDecodeSelWarps = kDecodeSelThreads / 32;
 constexpr int kDecodeMaxCap = 128;  // member slots per bucket the walk holds in registers
 
 template <typename TC>
-struct RawChunk;  // 8 consecutive elements of a centroid row, as loaded
+struct RawChunk;  // 8 consecutive elements of a centroid (or query) row, as loaded
 template <>
 struct RawChunk<__nv_bfloat16> {
     uint4 v;
@@ -737,6 +744,20 @@ struct RawChunk<__nv_bfloat16> {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             float2 f = __bfloat1622float2(h[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    }
+};
+template <>
+struct RawChunk<__half> {
+    uint4 v;
+    __device__ __forceinline__ void load(const __half* p) { v = __ldg(reinterpret_cast<const uint4*>(p)); }
+    __device__ __forceinline__ void get(float (&out)[8]) const {
+        const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f = __half22float2(h[i]);
             out[2 * i] = f.x;
             out[2 * i + 1] = f.y;
         }
@@ -807,6 +828,18 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
                    // the compiler issues all of them before the first use
         float x[CHUNKS][8];
         RawChunk<TC> raw[CPW][CHUNKS];
+        // a built query: thread i (< d / 8) owns index chunk i; its query rows are requested
+        // first, ahead of the centroid chunks (held raw, the first kGQ heads of the group)
+        constexpr int kGQ = GroupMeanOf<TQ>::value ? (sizeof(typename QRawOf<TQ>::type) == 4 ? 4 : 8) : 1;
+        RawChunk<typename QRawOf<TQ>::type> qraw[kGQ];
+        const typename QRawOf<TQ>::type* qbase = nullptr;
+        if constexpr (GroupMeanOf<TQ>::value) {
+            const int i = min((int)threadIdx.x, nchunks - 1);
+            const int j0 = i * 8, h = j0 / qg.D, e0 = j0 - h * qg.D;
+            qbase = reinterpret_cast<const typename QRawOf<TQ>::type*>(q) + r * ldq + (int64_t)h * qg.G * qg.D + e0;
+#pragma unroll
+            for (int g = 0; g < kGQ; ++g) qraw[g].load(qbase + (int64_t)min(g, qg.G - 1) * qg.D);
+        }
         if constexpr (!GroupMeanOf<TQ>::value) {
 #pragma unroll
             for (int j = 0; j < CHUNKS; ++j) {
@@ -829,20 +862,26 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
             // thread i builds chunk i (8 elements of one KV head) in shared memory
             using TR = typename GroupMeanOf<TQ>::raw;
             __shared__ __align__(16) float qsm[kDecodeMaxD];
-            const TR* qr = reinterpret_cast<const TR*>(q) + r * ldq;
-            for (int i = threadIdx.x; i < nchunks; i += kDecodeSelThreads) {
-                const int j0 = i * 8, h = j0 / qg.D, e0 = j0 - h * qg.D;
-                const TR* base = qr + (int64_t)h * qg.G * qg.D + e0;
+            if ((int)threadIdx.x < nchunks) {  // (kDecodeMaxD / 8 <= kDecodeSelThreads: one chunk a thread)
                 float acc[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-#pragma unroll 4
-                for (int g = 0; g < qg.G; ++g) {
+#pragma unroll
+                for (int g = 0; g < kGQ; ++g) {
+                    if (g < qg.G) {
+                        float v[8];
+                        qraw[g].get(v);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
+                    }
+                }
+                for (int g = kGQ; g < qg.G; ++g) {  // larger groups: the rest in order
                     float v[8];
-                    load8<TR>(base + (int64_t)g * qg.D, v);
+                    load8<TR>(qbase + (int64_t)g * qg.D, v);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], v[e]);
                 }
+                const int j0 = threadIdx.x * 8;
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     float m = __fdiv_rn(acc[e], (float)qg.G);
