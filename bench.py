@@ -237,6 +237,20 @@ def build_layers(dev, lsa, arms=False):
     return pcfg, layers
 
 
+def exchange_fn(world):
+    """The sharded legs' all-gather and its name: NCCL by default, or over peer memory (stores
+    into the peers' arenas over NVLink, lsa_b200.peer) with LSA_EXCHANGE=peer. Measured at two
+    GPUs: tree1m 168.5 us/step with NCCL, 176.5 with the peer gather; the batched split
+    selection 233 vs 242 us - the step's exchanges are latency-bound either way."""
+    from lsa_b200 import seqshard
+
+    if world == 1:
+        return (lambda x: x[None]), "none"
+    if os.environ.get("LSA_EXCHANGE", "nccl") == "peer":
+        return seqshard.peer_gather_fn(), "peer-memory"
+    return seqshard.all_gather_fn(), "NCCL"
+
+
 def run_b200(args, rank, world, dev):
     import torch
 
@@ -755,7 +769,7 @@ def run_batched(args, rank, world, dev, mode=None, dump=None):
     scale = DH ** -0.5
     stream = torch.cuda.Stream(dev)
     hkv_r = h1 - h0
-    gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
+    gather, exchange = exchange_fn(world)
 
     def select():
         if mode == "heads":
@@ -865,7 +879,7 @@ def run_batched(args, rank, world, dev, mode=None, dump=None):
                    "sequences_read_per_rank": nb, "heads_q": HQB, "heads_kv": HKV, "heads_kv_per_rank": hkv_r,
                    "head_dim": DH, "top_p_buckets": BATCH_CFG["top_p"], "budget_tokens": BATCH_CFG["top_k"],
                    "lengths": [len_lo, len_hi],
-                   "parallelism": {"heads": f"kv-head-shard{world} (selection split + NCCL all-gather of the lists)",
+                   "parallelism": {"heads": f"kv-head-shard{world} (selection split + {exchange} all-gather of the lists)",
                                    "heads_replicated": f"kv-head-shard{world} (selection replicated)",
                                    "sequences": f"sequence-shard{world}"}[mode],
                    "l2": "no flush: one step reads > 1 GB of K/V"},
@@ -910,7 +924,9 @@ def run_tree1m(args, rank, world, dev, dump=None):
     pcfg = lsa.PortConfig(**TREE_CFG)
     s0, s1 = seqshard.shard_bounds(C, world, rank, TREE_CFG["cluster_block_size"])
     n = s1 - s0
-    gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
+    gather, exchange = exchange_fn(world)
+    # the index build's one-time exchanges (member tables, MBs) go through NCCL
+    build_gather = seqshard.all_gather_fn() if world > 1 else (lambda x: x[None])
     pos = torch.full((1,), C - 1, dtype=torch.int32, device=dev)
     scale = DH ** -0.5
     sets = []
@@ -925,11 +941,11 @@ def run_tree1m(args, rank, world, dev, dump=None):
             k[b] = synthetic.drift_keys(n, HKV, DH, g, dev)[0].to(torch.bfloat16)
             v[b] = torch.randn(n, HKV, DH, generator=g, device=dev).to(torch.bfloat16)
             si = seqshard.build_shard_index(index_keys(k[b]), s0, pcfg)
-            rows = gather(torch.tensor([si.buckets.rows], dtype=torch.int64, device=dev))[:, 0].tolist()
+            rows = build_gather(torch.tensor([si.buckets.rows], dtype=torch.int64, device=dev))[:, 0].tolist()
             mine = seqshard.local_global_members(si)
             padded = torch.full((max(rows), mine.shape[1]), -1, dtype=torch.int32, device=dev)
             padded[: mine.shape[0]] = mine
-            tables = gather(padded)
+            tables = build_gather(padded)
             si.bucket_offset = sum(rows[:rank])
             si.members_global = torch.cat([tables[r][: rows[r]] for r in range(len(rows))]).contiguous()
             shards.append(si)
@@ -967,7 +983,7 @@ def run_tree1m(args, rank, world, dev, dump=None):
     torch.cuda.synchronize(dev)
     # each set's step captured in a CUDA graph (the step is a chain of small launches:
     # replaying removes the host's launch overhead); with several ranks the graph holds the
-    # two NCCL all-gathers too
+    # two all-gathers too
     use_graph = not args.tree_eager
     graphs = [None, None]
     stream = torch.cuda.Stream(dev)
@@ -1016,7 +1032,7 @@ def run_tree1m(args, rank, world, dev, dump=None):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded drift keys, N(0,1) q/v)",
         "config": {"workload": "tree1m", "batch": B, "context": C, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
-                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": "NCCL all-gather x2/step (candidates, partials)",
+                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": f"{exchange} all-gather x2/step (candidates, partials)",
                    "cuda_graph": use_graph, "rotation": "2 query/cache sets alternate step by step",
                    **{k2: TREE_CFG[k2] for k2 in ("bucket_size", "top_p", "top_k", "beam_width")},
                    "l2": "no flush: 2 sets of 4 x 1M-token caches (32 GiB) >> L2, consecutive steps read different sets"},

@@ -36,6 +36,26 @@ extern "C" {
 #define LSA_ERR_SHORT (-4)
 #define LSA_ERR_SIZE (-5)
 
+/* ---------------------------------------------------------------- peer-memory exchange */
+
+/* The sharded decode steps' all-gathers over peer memory (no reference counterpart: the
+ * reference is single-GPU; these replace torch.distributed.all_gather_into_tensor / NCCL for
+ * the small per-step exchanges). Each rank allocates an arena and shares its CUDA IPC handle
+ * (64 bytes); every rank opens every peer's handle. */
+int lsa_peer_arena_alloc(int64_t bytes, void** ptr, void* handle);
+int lsa_peer_arena_open(const void* handle, void** ptr);
+int lsa_peer_arena_close(void* ptr);
+int lsa_peer_arena_free(void* ptr);
+/* out [world][bytes] = every rank's src [bytes] (bytes a multiple of 16). bases[world]: every
+ * rank's arena as mapped in this process (bases[rank] = own); the channel's world uint32 flags
+ * at flag_off and its two receive buffers of world x bytes at recv_off in every arena; ctrl: 4
+ * device uint32 of this rank for the channel (zero at rest but the epoch). Two launches: the
+ * push stores into every rank's arena and publishes the epoch flag; the pull waits (bounded,
+ * 1 s; LSA_ERR_TIMEOUT in *status) for every rank's flag and copies the receive buffer out.
+ * Every rank makes the same sequence of calls per channel. CUDA-graph safe. */
+int lsa_peer_all_gather(const void* src, void* out, int64_t bytes, int rank, int world, void* const* bases,
+                        int64_t flag_off, int64_t recv_off, uint32_t* ctrl, int32_t* status, cudaStream_t stream);
+
 /* ---------------------------------------------------------------- index space */
 
 /* make_index_space -> upstream regroup (src/lsa_rocm_lab/port/gates.py:50-59).

@@ -42,6 +42,11 @@ SIGNATURES = {
     "lsa_expand_in_order": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
     "lsa_expand_from_keys": (_INT, [_P, _I, _I, _I, _P, _I, _I, _P, _I, _I, _I, _P, _P, _P]),
     "lsa_select_fused_scratch": (_I, [_I, _I]),
+    "lsa_peer_arena_alloc": (_INT, [_I, _P, _P]),
+    "lsa_peer_arena_open": (_INT, [_P, _P]),
+    "lsa_peer_arena_close": (_INT, [_P]),
+    "lsa_peer_arena_free": (_INT, [_P]),
+    "lsa_peer_all_gather": (_INT, [_P, _P, _I, _INT, _INT, _P, _I, _I, _P, _P, _P]),
     "lsa_select_fused_grouped": (_INT, [_P, _INT, _I, _I, _I, _I, _P, _INT, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I,
                                         _P, _P, _P]),
     "lsa_select_fused": (_INT, [_P, _INT, _I, _I, _P, _INT, _I, _I, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P, _P,

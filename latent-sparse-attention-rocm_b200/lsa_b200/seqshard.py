@@ -16,7 +16,8 @@ the buckets and node hierarchy of its own shard. A decode step has one exchange 
    (``lsa_sparse_read_partial``: fp32 output + log2-sum-exp per row and head);
 5. exchange: all-gather of the partials, and the log-sum-exp merge (``lsa_merge_partials``).
 
-The exchanges go through ``gather`` callables: ``torch.distributed.all_gather_into_tensor``
+The exchanges go through ``gather`` callables: ``peer_gather_fn`` (stores into the peers' memory
+over NVLink, ``lsa_b200.peer``), ``torch.distributed.all_gather_into_tensor``
 (NCCL over NVLink) across ranks, or a plain concatenation when one process emulates several
 shards. With one shard the procedure is exactly the single-GPU tree decode.
 """
@@ -196,6 +197,15 @@ def all_gather_fn(group=None):
         return out.view((world,) + tuple(x.shape))
 
     return gather
+
+
+def peer_gather_fn(group=None):
+    """A gather over ranks with the contract of ``all_gather_fn``, over peer memory: every rank
+    stores its chunk into every peer's arena over NVLink and waits for their flags (two small
+    kernels, ``lsa_b200.peer.PeerGather``; a collective to construct)."""
+    from .peer import PeerGather
+
+    return PeerGather(group)
 
 
 def seqshard_decode(q, k_shard, v_shard, index_queries, positions, s: ShardIndex, config, gather, scale=None):
