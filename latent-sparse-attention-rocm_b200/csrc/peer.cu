@@ -17,7 +17,7 @@
 // rank can only write gather e + 2 into a peer after that peer published e + 1, which the
 // peer does after its pull of gather e has copied the buffer out (stream order).
 // A flag that never arrives sets LSA_ERR_TIMEOUT in the status word and the pull returns.
-// No TMA and no multicast: plain stores and loads through the peer mappings.
+// Plain 16-byte stores and loads through the peer mappings only (no bulk or tensor copies).
 #include <cstring>
 
 #include "common.cuh"
