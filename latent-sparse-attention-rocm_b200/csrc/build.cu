@@ -247,7 +247,8 @@ __global__ void __launch_bounds__(kWardThreads) ward_merge_kernel(const float* _
     __shared__ int alive[kMaxP], sz[kMaxP], root[kMaxP], nn[kMaxP], partner[kMaxP], dying[kMaxP], into[kMaxP];
     __shared__ int64_t nnkey[kMaxP], pkey[kMaxP];
     __shared__ int pa[kMaxP];
-    __shared__ int m_pairs, count;
+    __shared__ int fresh[kMaxP], olist[kMaxP];  // merged last round / this round's merging owners
+    __shared__ int m_pairs, count, n_own, n_fresh;
     const int blk = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const float* src = gram + (int64_t)blk * P * P;
     for (int i = tid; i < P * P; i += blockDim.x) G[i] = src[i];
@@ -255,27 +256,54 @@ __global__ void __launch_bounds__(kWardThreads) ward_merge_kernel(const float* _
         alive[i] = 1;
         sz[i] = sizes0[(int64_t)blk * P + i];
         root[i] = i;
+        fresh[i] = 0;
+        nn[i] = -1;
     }
-    if (tid == 0) count = P;
+    if (tid == 0) {
+        count = P;
+        n_fresh = -1;  // the first round searches every cluster's partner
+    }
     __syncthreads();
+    // the Ward cost of clusters i and j (packed with j): the same arithmetic for every search
+    auto key_of = [&](int i, int j, float gii) -> int64_t {
+        const float merged = __fadd_rn(__fadd_rn(gii, G[j * P + j]), __fmul_rn(2.0f, G[i * P + j]));
+        const float cost = __fsub_rn(__fadd_rn(norm[i], norm[j]), __fsqrt_rn(fmaxf(merged, 0.0f)));
+        return pack_cost(cost, j);
+    };
     while (count > target) {
         for (int i = tid; i < P; i += blockDim.x) {
             norm[i] = alive[i] ? __fsqrt_rn(G[i * P + i]) : 0.0f;
             partner[i] = -1;
             dying[i] = 0;
         }
-        if (tid == 0) m_pairs = 0;
+        if (tid == 0) {
+            m_pairs = 0;
+            n_own = 0;
+        }
         __syncthreads();
-        // nearest feasible partner of every alive cluster (min packed cost|j)
+        // nearest feasible partner of every alive cluster (min packed cost|j). A cluster that
+        // merged last round, or whose partner merged or was absorbed, searches all clusters;
+        // for any other the kept key is still exact (its costs to unchanged clusters did not
+        // change) and only last round's merged clusters can beat it.
+        const int nf = n_fresh;
         for (int i = warp; i < P; i += nw) {
+            if (!alive[i]) continue;  // (warp-uniform)
+            const int ni = nn[i];
+            const bool all = nf < 0 || fresh[i] || ni < 0 || !alive[ni] || fresh[ni];
+            const float gii = G[i * P + i];
             int64_t best = INT64_MAX;
-            if (alive[i]) {
-                float gii = G[i * P + i];
+            if (all) {
                 for (int j = lane; j < P; j += 32) {
                     if (j == i || !alive[j] || sz[i] + sz[j] > cap) continue;
-                    float merged = __fadd_rn(__fadd_rn(gii, G[j * P + j]), __fmul_rn(2.0f, G[i * P + j]));
-                    float cost = __fsub_rn(__fadd_rn(norm[i], norm[j]), __fsqrt_rn(fmaxf(merged, 0.0f)));
-                    int64_t key = pack_cost(cost, j);
+                    const int64_t key = key_of(i, j, gii);
+                    best = key < best ? key : best;
+                }
+            } else {
+                if (lane == 0) best = nnkey[i];
+                for (int x = lane; x < nf; x += 32) {
+                    const int j = olist[x];
+                    if (j == i || !alive[j] || sz[i] + sz[j] > cap) continue;
+                    const int64_t key = key_of(i, j, gii);
                     best = key < best ? key : best;
                 }
             }
@@ -310,15 +338,19 @@ __global__ void __launch_bounds__(kWardThreads) ward_merge_kernel(const float* _
                 partner[a] = b;
                 dying[b] = 1;
                 into[b] = a;
+                olist[atomicAdd(&n_own, 1)] = a;
             }
         }
         __syncthreads();
-        // batched Gram update of surviving pairs, from the previous matrix
-        for (int idx = tid; idx < P * P; idx += blockDim.x) {
-            int A = idx / P, C = idx % P;
-            if (C < A || !alive[A] || !alive[C] || dying[A] || dying[C]) continue;
-            int b = partner[A], dd = partner[C];
-            if (b < 0 && dd < 0) continue;
+        // batched Gram update, from the previous matrix: every pair (A <= C) of surviving
+        // clusters with at least one merging owner, each visited once (two owners: from the
+        // lower one), with A the lower index as the update's arithmetic is written
+        const int no = n_own;
+        for (int idx = tid; idx < no * P; idx += blockDim.x) {
+            const int a1 = olist[idx / P], X = idx % P;
+            if (!alive[X] || dying[X] || (partner[X] >= 0 && X < a1)) continue;
+            const int A = a1 < X ? a1 : X, C = a1 < X ? X : a1;
+            const int b = partner[A], dd = partner[C];
             float val;
             if (A == C) {
                 val = __fadd_rn(__fadd_rn(G[A * P + A], G[A * P + b]), __fadd_rn(G[b * P + A], G[b * P + b]));
@@ -332,11 +364,11 @@ __global__ void __launch_bounds__(kWardThreads) ward_merge_kernel(const float* _
             G2[A * P + C] = val;
         }
         __syncthreads();
-        for (int idx = tid; idx < P * P; idx += blockDim.x) {
-            int A = idx / P, C = idx % P;
-            if (C < A || !alive[A] || !alive[C] || dying[A] || dying[C]) continue;
-            if (partner[A] < 0 && partner[C] < 0) continue;
-            float val = G2[A * P + C];
+        for (int idx = tid; idx < no * P; idx += blockDim.x) {
+            const int a1 = olist[idx / P], X = idx % P;
+            if (!alive[X] || dying[X] || (partner[X] >= 0 && X < a1)) continue;
+            const int A = a1 < X ? a1 : X, C = a1 < X ? X : a1;
+            const float val = G2[A * P + C];
             G[A * P + C] = val;
             G[C * P + A] = val;
         }
@@ -347,14 +379,13 @@ __global__ void __launch_bounds__(kWardThreads) ward_merge_kernel(const float* _
             if (dying[rt]) root[i] = into[rt];
         }
         __syncthreads();
+        for (int i = tid; i < P; i += blockDim.x) {
+            fresh[i] = partner[i] >= 0;
+            if (dying[i]) alive[i] = 0;
+        }
         if (tid == 0) {
-            int merged = 0;
-            for (int i = 0; i < P; ++i)
-                if (dying[i]) {
-                    alive[i] = 0;
-                    ++merged;
-                }
-            count -= merged;
+            count -= no;  // each merge absorbs one cluster
+            n_fresh = no;
         }
         __syncthreads();
     }
