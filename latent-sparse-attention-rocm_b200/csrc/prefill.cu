@@ -23,12 +23,13 @@
 // flight beat TMA row gathers here: a tile::gather4 moves 512 B and the copy engine takes
 // roughly 75 cycles per gather, about 7 B/clk per SM.
 // Each half has its own MMA issuing warp: S_h(j), then PV_h(j) in two parts as the half's
-// softmax publishes P_h(j) for the first and the last 64 keys, then S_h(j+1); the tensor pipe interleaves the two halves, so one half's
-// MMAs run while the other half's softmax works. tcgen05 operations of one thread run in
-// order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and O_h is current
-// whenever the softmax sees S_h(j+1). Two issuers because one thread issues one MMA per
-// ~180 cycles (measured on B200: 128 x 128 x 16 MMAs from one thread reach half the pipe's
-// rate, from two threads all of it).
+// softmax publishes P_h(j) for the first and the last 64 keys, then S_h(j+1). The two
+// softmax warpgroups take turns (h0 chunk j, h1 chunk j, h0 chunk j+1, ...), so one half's
+// exponentials run while the tensor pipe runs the other half's MMAs. tcgen05 operations of
+// one thread run in order, so S_h(j+1) overwrites P_h(j) only after PV_h(j) has read it, and
+// O_h is current whenever the softmax sees S_h(j+1). Two issuers because one thread issues
+// one MMA per ~180 cycles (measured on B200: 128 x 128 x 16 MMAs from one thread reach half
+// the pipe's rate, from two threads all of it).
 // Warp roles (16 warps): warps 0 / 1 issue half 0's / half 1's MMAs (warp 0 also owns the
 // TMEM allocation); warps 2-3 and 12-15 load Q, K and V; warps 4-7 / 8-11 run the softmax of
 // half 0 / half 1.
