@@ -13,7 +13,11 @@
 // Ward merge, one CTA per cluster block, Gram matrix resident in shared memory:
 //   rounds of mutual nearest partners under the size cap (packed int64 cost|index keys),
 //   cheapest mutual pairs merged first, at most count - target per round, all merges of
-//   a round applied together from the previous Gram matrix.
+//   a round applied together from the previous Gram matrix. The rounds are incremental: a
+//   cluster searches every partner only when it or its partner changed in the last round,
+//   and the Gram update visits only the pairs of a merging cluster - the same keys and
+//   values as recomputing everything.
+// k == nullptr in the regroup kernels: index queries only.
 #include "common.cuh"
 
 namespace lsa {
