@@ -803,18 +803,29 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
     // first cluster phase: every CTA has started before any of them writes the leader's
     // shared memory (waited on just before that store)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-    if (rp.table_off == nullptr) {
-        // the index is read-only here: pull this warp's centroid and member rows into L2
-        // while the previous kernel finishes
-        const int clines = (int)((int64_t)d * sizeof(TC) / 128);
+    // One table (no per-row offsets, the decode rows): the index is read-only here, and the
+    // kernels that write centroids or member rows (the builds, table copies) never trigger
+    // their dependents early, so this grid starts only after they completed - the warp's
+    // centroid chunks are loaded into registers before griddepcontrol.wait (overlapping the
+    // previous kernel, in a decode step the previous layer's read) and its member rows pulled
+    // into L2. Only the query, which the previous kernel may produce, is read after the wait.
+    // (only where the chunks fit in 32 registers: wider tiles keep the loads after the wait,
+    // where the compiler may interleave them with the FMAs instead of spilling)
+    constexpr bool kEarlyFits = CPW * CHUNKS * sizeof(RawChunk<TC>) <= 128;
+    const bool early = kEarlyFits && rp.table_off == nullptr;
+    RawChunk<TC> raw[CPW][CHUNKS];
+    if (early && Nr > 0) {
 #pragma unroll
         for (int i = 0; i < CPW; ++i) {
-            const int64_t n = c0 + warp + kDecodeSelWarps * i;
-            if (n < Nr) {
-                const char* base = reinterpret_cast<const char*>(c + n * d);
-                for (int l = lane; l < clines; l += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + l * 128));
-                if (lane < mlines) asm volatile("prefetch.global.L2 [%0];" ::"l"(members + n * cap + lane * 32));
+            int64_t n = c0 + warp + kDecodeSelWarps * i;
+            n = n < Nr ? n : Nr - 1;  // a valid row; masked below
+#pragma unroll
+            for (int j = 0; j < CHUNKS; ++j) {
+                const int ch = min(lane + 32 * j, nchunks - 1);
+                raw[i][j].load(c + n * d + (size_t)ch * 8);
             }
+            if (n == c0 + warp + kDecodeSelWarps * i && lane < mlines)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(members + n * cap + lane * 32));
         }
     }
     pdl_wait();
@@ -827,7 +838,6 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
     if (Nr > 0) {  // (block-uniform) loads are unconditional, at clamped valid addresses, so
                    // the compiler issues all of them before the first use
         float x[CHUNKS][8];
-        RawChunk<TC> raw[CPW][CHUNKS];
         // a built query: thread i (< d / 8) owns index chunk i; its query rows are requested
         // first, ahead of the centroid chunks (held raw, the first kGQ heads of the group)
         constexpr int kGQ = GroupMeanOf<TQ>::value ? (sizeof(typename QRawOf<TQ>::type) == 4 ? 4 : 8) : 1;
@@ -847,14 +857,16 @@ __global__ void __launch_bounds__(kDecodeSelThreads) select_decode_kernel(
                 load8<TQ>(q + r * ldq + (size_t)ch * 8, x[j]);
             }
         }
+        if (!early) {
 #pragma unroll
-        for (int i = 0; i < CPW; ++i) {
-            int64_t n = c0 + warp + kDecodeSelWarps * i;
-            n = n < Nr ? n : Nr - 1;  // a valid row; masked below
+            for (int i = 0; i < CPW; ++i) {
+                int64_t n = c0 + warp + kDecodeSelWarps * i;
+                n = n < Nr ? n : Nr - 1;  // a valid row; masked below
 #pragma unroll
-            for (int j = 0; j < CHUNKS; ++j) {
-                const int ch = min(lane + 32 * j, nchunks - 1);
-                raw[i][j].load(cr + n * d + (size_t)ch * 8);
+                for (int j = 0; j < CHUNKS; ++j) {
+                    const int ch = min(lane + 32 * j, nchunks - 1);
+                    raw[i][j].load(cr + n * d + (size_t)ch * 8);
+                }
             }
         }
         if constexpr (GroupMeanOf<TQ>::value) {
