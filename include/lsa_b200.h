@@ -274,6 +274,23 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
                          int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
                          int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream);
 
+/* tree_select with its expansion (src/lsa_rocm_lab/port/_tree.py:34-60: the beam's picks, then
+ * expand_in_order into read lists): lsa_tree_select's picks plus lists [R, top_k + window +
+ * sink] int32 (-1 padded) and lengths [R] int32, equal to lsa_expand_in_order(picks, R, top_p,
+ * top_p, members, ...). members [member_rows, cap] int32. One launch when the beam's cluster
+ * form takes the call (<= 64 rows) and top_p * cap + top_k slots fit 128 KB of shared memory,
+ * else the beam and the expansion kernel. Scratch / counters as lsa_tree_plan reports. The
+ * launch reads positions (and the read-only index) before it waits for the previous kernel
+ * in the stream: a kernel that writes them must not let its dependents start early. */
+int lsa_tree_select_lists(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                          int64_t rows, int64_t n_built, const float* const* level_centroids,
+                          const int64_t* const* level_children, const int64_t* level_counts,
+                          const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                          int64_t top_p, const int32_t* members, int64_t member_rows, int64_t cap, int64_t window,
+                          int64_t sink, int64_t top_k, int32_t* picks, int32_t* lists, int32_t* lengths,
+                          void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                          cudaStream_t stream);
+
 /* ---------------------------------------------------------------- read */
 
 /* Split plan of lsa_sparse_read: splits per (row, KV head), scratch bytes, counters (the

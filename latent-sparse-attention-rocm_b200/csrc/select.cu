@@ -19,12 +19,19 @@
 #include "common.cuh"
 #include "topk.cuh"
 #include "umma.cuh"
+#include "walk.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace lsa {
 
 constexpr int kSortCap = 8192;  // keys sorted in one shared-memory pass (64 KB)
+
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while the previous kernel runs; griddepcontrol.wait blocks until that kernel
+// has completed and its memory is visible, launch_dependents lets the next kernel start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------------------------ scoring
 
@@ -261,6 +268,8 @@ __global__ void __launch_bounds__(512) expand_kernel(const PickT* __restrict__ p
                                                      int top_k, int32_t* __restrict__ lists,
                                                      int32_t* __restrict__ lengths) {
     __shared__ int scan_smem[33];
+    pdl_wait();  // the picks are the previous kernel's output
+    pdl_trigger();
     int r = blockIdx.x;
     int width = top_k + window + sink;
     if constexpr (sizeof(PickT) == 8) {
@@ -322,9 +331,6 @@ template <typename T, bool RB> struct QRawOf<GroupMean<T, RB>> {
 constexpr int kMemberPrefetch = 8192;  // member slots staged in shared memory in one round trip
 constexpr int kGatherMax = 8192;       // read-list slots the fused selects gather in shared memory
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 // Descending bitonic sort of one key per thread across the block (blockDim.x a power of
 // two); returns the key of rank threadIdx.x. Strides below 32 exchange by warp shuffles,
 // larger strides through shared memory (xchg: blockDim.x int64).
@@ -347,76 +353,6 @@ __device__ __forceinline__ int64_t block_bitonic_desc_regs(int64_t x, int64_t* x
         }
     }
     return x;
-}
-
-// The rank-order walk over staged member slots mem[0, total) (slot p * cap + m holds member
-// m of the p-th pick; -1 and ids outside [sink, ws) are skipped): one scan over all slots
-// gives every thread its output offset, kept ids go out in slot order up to top_k, then the
-// window [ws, pos] and the sinks [0, min(sink, ws)). Run by NT threads (tid in [0, NT)) that
-// share the barrier `sync`; mem must be 16-byte aligned.
-template <int NT, typename Sync>
-__device__ void expand_walk(const int* mem, int total, int64_t pos, int window, int sink, int top_k,
-                            int32_t* __restrict__ out, int width, int32_t* length_out, int* scan_smem, int tid,
-                            Sync sync, int* gather = nullptr) {
-    // gather (top_k ints of shared memory, optional): kept ids land there first and leave in
-    // one coalesced copy instead of scattered 4-byte stores per thread
-    int32_t* dst = gather ? gather : out;
-    int64_t ws = pos + 1 - window;
-    if (ws < 0) ws = 0;
-    auto keep = [&](int v) { return v >= 0 && v >= sink && (int64_t)v < ws; };
-    const int spt = (total + NT - 1) / NT;
-    const int first = tid * spt;
-    const bool vec = spt % 4 == 0 && first + spt <= total;  // contiguous 16-byte reads of this thread's slots
-    int cnt = 0;
-    if (vec) {
-        for (int i = 0; i < spt; i += 4) {
-            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
-            cnt += keep(v.x) + keep(v.y) + keep(v.z) + keep(v.w);
-        }
-    } else {
-        for (int i = 0; i < spt; ++i) {
-            int s = first + i;
-            cnt += (s < total && keep(mem[s]));
-        }
-    }
-    int filled;
-    int at = group_exclusive_scan<NT>(cnt, scan_smem, &filled, tid, sync);
-    if (vec) {
-        for (int i = 0; i < spt && at < top_k; i += 4) {
-            int4 v = *reinterpret_cast<const int4*>(mem + first + i);
-            const int e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (keep(e[u])) {
-                    if (at < top_k) dst[at] = e[u];
-                    ++at;
-                }
-            }
-        }
-    } else {
-        for (int i = 0; i < spt && at < top_k; ++i) {
-            int s = first + i;
-            if (s < total && keep(mem[s])) {
-                dst[at] = mem[s];
-                ++at;
-            }
-        }
-    }
-    if (filled > top_k) filled = top_k;
-    if (gather) {
-        sync();
-        for (int i = tid; i < filled; i += NT) out[i] = gather[i];
-    }
-    int nwin = (int)(pos - ws + 1);
-    if (nwin < 0) nwin = 0;
-    int nsink = (int)(sink < ws ? sink : ws);
-    for (int i = tid; i < width - filled; i += NT) {
-        int j = filled + i, v = -1;
-        if (i < nwin) v = (int)(ws + i);
-        else if (i < nwin + nsink) v = i - nwin;
-        out[j] = v;
-    }
-    if (tid == 0) *length_out = filled + nwin + nsink;
 }
 
 struct BlockSync {
@@ -472,6 +408,8 @@ __global__ void __launch_bounds__(512) expand_staged_kernel(const PickT* __restr
                                                             int32_t* __restrict__ lengths, int vec16) {
     extern __shared__ __align__(16) int esm[];
     __shared__ int scan_smem[33];
+    pdl_wait();  // the picks are the previous kernel's output
+    pdl_trigger();
     const int total = P * cap;
     int* mem = esm;
     int* gather = esm + ((total + 3) & ~3);
@@ -1406,31 +1344,40 @@ int64_t lsa_select_fused_scratch(int64_t R, int64_t N) { return ((R * N * 8 + 25
 static int expand_launch(bool keys64, const void* picks, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
                          int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
                          int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream) {
+    // programmatic dependent launch: the kernels wait for the picks' producer before any read
+    cudaLaunchAttribute pdl;
+    pdl.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)R);
+    lc.blockDim = dim3(512);
+    lc.stream = stream;
+    lc.attrs = &pdl;
+    lc.numAttrs = 1;
+    cudaError_t e;
     const int64_t staged = ((P * cap + 3) / 4 * 4 + top_k) * 4;
     if (staged <= 200 * 1024 && P * cap < (1 << 30)) {
         const int vec16 = cap % 4 == 0 && aligned16(members);
+        lc.dynamicSmemBytes = (size_t)staged;
         if (keys64) {
             auto kern = expand_staged_kernel<int64_t>;
             if (set_smem(kern, (int)staged)) return LSA_ERR_CUDA;
-            kern<<<(unsigned)R, 512, (size_t)staged, stream>>>((const int64_t*)picks, (int)P, ldp, members, member_rows,
-                                                              (int)cap, positions, (int)window, (int)sink, (int)top_k,
-                                                              lists, lengths, vec16);
+            e = cudaLaunchKernelEx(&lc, kern, (const int64_t*)picks, (int)P, ldp, members, member_rows, (int)cap,
+                                   positions, (int)window, (int)sink, (int)top_k, lists, lengths, vec16);
         } else {
             auto kern = expand_staged_kernel<int32_t>;
             if (set_smem(kern, (int)staged)) return LSA_ERR_CUDA;
-            kern<<<(unsigned)R, 512, (size_t)staged, stream>>>((const int32_t*)picks, (int)P, ldp, members, member_rows,
-                                                              (int)cap, positions, (int)window, (int)sink, (int)top_k,
-                                                              lists, lengths, vec16);
+            e = cudaLaunchKernelEx(&lc, kern, (const int32_t*)picks, (int)P, ldp, members, member_rows, (int)cap,
+                                   positions, (int)window, (int)sink, (int)top_k, lists, lengths, vec16);
         }
     } else if (keys64) {
-        expand_kernel<int64_t><<<(unsigned)R, 512, 0, stream>>>((const int64_t*)picks, (int)P, ldp, members,
-                                                               member_rows, (int)cap, positions, (int)window,
-                                                               (int)sink, (int)top_k, lists, lengths);
+        e = cudaLaunchKernelEx(&lc, expand_kernel<int64_t>, (const int64_t*)picks, (int)P, ldp, members, member_rows,
+                               (int)cap, positions, (int)window, (int)sink, (int)top_k, lists, lengths);
     } else {
-        expand_kernel<int32_t><<<(unsigned)R, 512, 0, stream>>>((const int32_t*)picks, (int)P, ldp, members,
-                                                               member_rows, (int)cap, positions, (int)window,
-                                                               (int)sink, (int)top_k, lists, lengths);
+        e = cudaLaunchKernelEx(&lc, expand_kernel<int32_t>, (const int32_t*)picks, (int)P, ldp, members, member_rows,
+                               (int)cap, positions, (int)window, (int)sink, (int)top_k, lists, lengths);
     }
+    if (e != cudaSuccess) return LSA_ERR_CUDA;
     LSA_LAUNCH_CHECK();
     return LSA_OK;
 }

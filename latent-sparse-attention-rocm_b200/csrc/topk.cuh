@@ -132,14 +132,20 @@ __device__ __forceinline__ void warp_merge_desc(int64_t (&x)[KW], const int64_t 
 }
 
 // The K = 32 * KW greatest of key(0 .. n) (EMPTY past n), sorted descending, into out[0, K),
-// by NW warps (warp in [0, NW)) that share the barrier `sync`. Every warp folds its K-key
-// chunks into one sorted list (the next chunk's loads in flight while the current one
-// sorts), then a merge tree over the warps' lists. lists: NW * K int64 of shared memory.
+// by NW warps (warp in [0, NW)) that share the barrier `sync` (n the same in every warp).
+// Every warp whose first K-key chunk holds keys folds its chunks into one sorted list (the
+// next chunk's loads in flight while the current one sorts); the merge tree then runs over
+// those warps' lists only - the other warps' lists would be all EMPTY, and merging one in
+// changes nothing - so few keys take few merge levels and the idle warps take no issue
+// slots from the sorting ones. lists: NW * K int64 of shared memory.
 template <int KW, int NW, typename Loader, typename Sync>
 __device__ __forceinline__ void group_topk_desc(const Loader& key, int n, int64_t* lists, int64_t* out, int warp,
                                                 int lane, Sync sync) {
     constexpr int K = 32 * KW;
+    const int nl = n <= 0 ? 0 : ((n + K - 1) / K < NW ? (n + K - 1) / K : NW);  // warps holding keys
     int64_t x[KW], nx[KW];
+#pragma unroll
+    for (int w = 0; w < KW; ++w) x[w] = kEmpty;
     auto load = [&](int chunk, int64_t (&y)[KW]) {
 #pragma unroll
         for (int w = 0; w < KW; ++w) {
@@ -147,23 +153,25 @@ __device__ __forceinline__ void group_topk_desc(const Loader& key, int n, int64_
             y[w] = i < n ? key(i) : kEmpty;
         }
     };
-    load(warp, x);
-    if ((warp + NW) * K < n) load(warp + NW, nx);
-    warp_sort_desc<KW>(x, lane);
-    for (int c = warp + NW; c * K < n; c += NW) {
-        int64_t y[KW];
+    if (warp < nl) {
+        load(warp, x);
+        if ((warp + NW) * K < n) load(warp + NW, nx);
+        warp_sort_desc<KW>(x, lane);
+        for (int c = warp + NW; c * K < n; c += NW) {
+            int64_t y[KW];
 #pragma unroll
-        for (int w = 0; w < KW; ++w) y[w] = nx[w];
-        if ((c + NW) * K < n) load(c + NW, nx);
-        warp_sort_desc<KW>(y, lane);
-        warp_merge_desc<KW>(x, y, lane);
+            for (int w = 0; w < KW; ++w) y[w] = nx[w];
+            if ((c + NW) * K < n) load(c + NW, nx);
+            warp_sort_desc<KW>(y, lane);
+            warp_merge_desc<KW>(x, y, lane);
+        }
+#pragma unroll
+        for (int w = 0; w < KW; ++w) lists[warp * K + w * 32 + lane] = x[w];
     }
-#pragma unroll
-    for (int w = 0; w < KW; ++w) lists[warp * K + w * 32 + lane] = x[w];
     sync();
-#pragma unroll
-    for (int step = 1; step < NW; step <<= 1) {
-        if ((warp % (2 * step)) == 0 && warp + step < NW) {
+#pragma unroll 1
+    for (int step = 1; step < nl; step <<= 1) {
+        if ((warp % (2 * step)) == 0 && warp + step < nl) {
 #pragma unroll
             for (int w = 0; w < KW; ++w) {
                 const int64_t y = lists[(warp + step) * K + K - 1 - (w * 32 + lane)];

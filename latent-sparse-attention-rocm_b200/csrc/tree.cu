@@ -22,6 +22,8 @@
 
 #include "common.cuh"
 #include "topk.cuh"
+#include "umma.cuh"
+#include "walk.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -195,19 +197,28 @@ __global__ void __launch_bounds__(256) tree_level_kernel(TreeLevelArgs a) {
 // One thread-block cluster per row walks every level in ONE launch (the multi-launch form
 // above pays a launch, a ticket round trip and a global key round trip per level):
 //   * before griddepcontrol.wait the cluster pulls every node level's centroid rows into L2
-//     (the hierarchy is read-only here; prefetches cannot observe stale data);
+//     (the index is read-only here; prefetches cannot observe stale data), and reads the
+//     row's position and derives its growth: positions are inputs of the step, which no
+//     kernel of this library writes (the ones that let their dependents start early write
+//     lists, keys, picks, index queries or outputs); only the index query, which the
+//     previous kernel may produce, is read after the wait;
 //   * per level, every CTA derives the level's candidate count from the row's growth and the
 //     previous level's kept count (the same arithmetic in every CTA), scores its share of the
-//     candidates (one warp per candidate, canonical fp32 cdot, the row's query in registers;
+//     candidates (one warp per two candidates, both rows' loads in flight before the FMAs,
+//     canonical fp32 cdot, the row's query staged in shared memory;
 //     carried ids read from the leader's shared memory through DSMEM) and stores the packed
 //     keys into the leader's shared memory;
 //   * one cluster barrier; the leader keeps the best beam_width (top_p at level 0) by warp-list
 //     top-K and writes the next level's carried children into its shared memory; a second
-//     barrier publishes them. Level 0 writes the picks (and their rebased keys).
+//     barrier publishes them. Level 0 writes the picks (and their rebased keys) and, for
+//     lsa_tree_select_lists, walks the expansion in the leader: the picked member rows staged
+//     in shared memory by 16-byte cp.async (one round trip), then the same walk as the
+//     expansion kernel - read lists without a second launch.
 // Same picks as the multi-launch form (same candidates, same keys, same order).
 constexpr int kTreeCThreads = 512;
 constexpr int kTreeCWarps = kTreeCThreads / 32;
 constexpr int kTreeCMaxCand = 4096;
+constexpr int kTreeMaxD = 2048;                     // index dims (the entry points check d)
 
 struct TreeClusterArgs {
     const float* q;
@@ -224,6 +235,13 @@ struct TreeClusterArgs {
     int64_t col_offset;
     int cand_cap, carry_cap;
     int32_t* status;
+    // the expansion walk (lists != null): members [member_rows, cap], staged at byte offset
+    // stage_off of the dynamic shared memory
+    const int32_t* members;
+    int64_t member_rows;
+    int cap, window, sink, top_k, vec16, stage_off;
+    int32_t* lists;
+    int32_t* lengths;
 };
 
 struct SmemKeys {
@@ -231,6 +249,56 @@ struct SmemKeys {
     int n;
     __device__ int64_t operator()(int i) const { return i < n ? k[i] : kEmpty; }
 };
+
+// One candidate row's lane chunks (fp32, 8 per chunk; chunks past nchunks are not read)
+// and the lane's partial of the canonical cdot over them - the order of lane_partial_regs,
+// split so two rows' loads can be in flight before either row's FMAs.
+template <int CHUNKS>
+__device__ __forceinline__ void load_row_chunks(const float* y, int lane, int nchunks, float (&v)[CHUNKS][8]) {
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunks) load8<float>(y + (size_t)c * 8, v[j]);
+    }
+}
+// The lane's partial of one row against the query staged in shared memory (qs), in the
+// order of lane_partial_regs (chunk by chunk, element by element).
+template <int CHUNKS>
+__device__ __forceinline__ float lane_partial1(const float* qs, const float (&v)[CHUNKS][8], int lane, int nchunks) {
+    float p = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunks) {
+            float xv[8];
+            load8<float>(qs + (size_t)c * 8, xv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p = __fmaf_rn(xv[e], v[j][e], p);
+        }
+    }
+    return p;
+}
+// The same for two rows at once (one query chunk read feeds both).
+template <int CHUNKS>
+__device__ __forceinline__ void lane_partials2(const float* qs, const float (&v1)[CHUNKS][8],
+                                               const float (&v2)[CHUNKS][8], int lane, int nchunks, float& p1,
+                                               float& p2) {
+    p1 = 0.0f;
+    p2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < CHUNKS; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunks) {
+            float xv[8];
+            load8<float>(qs + (size_t)c * 8, xv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                p1 = __fmaf_rn(xv[e], v1[j][e], p1);
+                p2 = __fmaf_rn(xv[e], v2[j][e], p2);
+            }
+        }
+    }
+}
 
 __device__ __forceinline__ void tc_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tc_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
@@ -256,19 +324,17 @@ __global__ void __launch_bounds__(kTreeCThreads) tree_cluster_kernel(const TreeC
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(a.lc[l] + n * a.d) +
                                                                   i * 128));
     }
-    pdl_wait();
-    pdl_trigger();
     const int64_t pos = a.positions[r];
     const int64_t page = pos / a.block;
     TreeGrowth g;
     growth_at(page, a.bpb, a.nb, a.size, a.top_level, a.rows, a.n_built, g);
+    pdl_wait();
+    pdl_trigger();
     const int nchunks = (int)(a.d >> 3);
-    float x[CHUNKS][8];
-#pragma unroll
-    for (int j = 0; j < CHUNKS; ++j) {
-        const int ch = min(lane + 32 * j, nchunks - 1);
-        load8<float>(a.q + r * a.d + (size_t)ch * 8, x[j]);
-    }
+    __shared__ __align__(16) float qs[kTreeMaxD];
+    for (int i = threadIdx.x; i < nchunks * 2; i += kTreeCThreads)
+        reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(a.q + r * a.d)[i];
+    __syncthreads();
     int64_t* lead_keys = cluster.map_shared_rank(keys, 0);
     const int32_t* lead_carried = cluster.map_shared_rank(carried, 0);
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // (first phase)
@@ -297,19 +363,54 @@ __global__ void __launch_bounds__(kTreeCThreads) tree_cluster_kernel(const TreeC
             n_cand = a.cand_cap;
         }
         const float* cent = L > 0 ? a.lc[L - 1] : a.bc;
-        for (int i = rank * kTreeCWarps + warp; i < n_cand; i += cs * kTreeCWarps) {
+        // two candidates per warp pass (both rows' loads in flight before the FMAs) while two
+        // rows fit the registers (d <= 1024), else one
+        constexpr int PAIR = CHUNKS <= 4 ? 2 : 1;
+        const int stride = cs * kTreeCWarps;
+        for (int i = rank * kTreeCWarps + warp; i < n_cand; i += PAIR * stride) {
             const int id = i < n_carried ? lead_carried[i] : fresh0 + (i - n_carried);
-            const float s = butterfly_sum(lane_partial_regs<float, CHUNKS>(x, cent + (int64_t)id * a.d, lane, nchunks));
-            if (lane == 0) lead_keys[i] = pack_key(s, id);
+            float v1[CHUNKS][8];
+            if constexpr (PAIR == 2) {
+                const int i2 = i + stride;
+                const bool two = i2 < n_cand;  // (warp-uniform)
+                const int id2 = !two ? id : (i2 < n_carried ? lead_carried[i2] : fresh0 + (i2 - n_carried));
+                float v2[CHUNKS][8];
+                load_row_chunks<CHUNKS>(cent + (int64_t)id * a.d, lane, nchunks, v1);
+                load_row_chunks<CHUNKS>(cent + (int64_t)id2 * a.d, lane, nchunks, v2);
+                float p1, p2;
+                lane_partials2<CHUNKS>(qs, v1, v2, lane, nchunks, p1, p2);
+                const float s1 = butterfly_sum(p1);
+                const float s2 = butterfly_sum(p2);
+                if (lane == 0) {
+                    lead_keys[i] = pack_key(s1, id);
+                    if (two) lead_keys[i2] = pack_key(s2, id2);
+                }
+            } else {
+                load_row_chunks<CHUNKS>(cent + (int64_t)id * a.d, lane, nchunks, v1);
+                const float s1 = butterfly_sum(lane_partial1<CHUNKS>(qs, v1, lane, nchunks));
+                if (lane == 0) lead_keys[i] = pack_key(s1, id);
+            }
         }
         tc_arrive();
         const int keep = L > 0 ? a.beam : a.top_p;
         const int kept = n_cand < keep ? n_cand : keep;
         if (L == 0 && rank != 0) return;  // nothing of this CTA is read after the last scores
         tc_wait();
+        // a node level whose candidates all stay needs no top-K: only the kept SET matters
+        // below it (the next level's keys carry the bucket / node id, so the carried order
+        // cannot change any pick), and the keys are read in place
+        const bool all_kept = L > 0 && n_cand <= keep;
         if (rank == 0) {
-            group_topk_desc<KW, kTreeCWarps>(SmemKeys{keys, n_cand}, n_cand, lists, best, warp, lane,
-                                             TreeBlockSync{});
+            // the picks of a top_p <= 32 walk: 32-key warp lists (half the sort work of the
+            // beam's wider lists; the same best 32 keys in the same order)
+            bool narrow = false;
+            if constexpr (KW > 1) narrow = L == 0 && a.top_p <= 32;
+            if (narrow)
+                group_topk_desc<1, kTreeCWarps>(SmemKeys{keys, n_cand}, n_cand, lists, best, warp, lane,
+                                                TreeBlockSync{});
+            else if (!all_kept)
+                group_topk_desc<KW, kTreeCWarps>(SmemKeys{keys, n_cand}, n_cand, lists, best, warp, lane,
+                                                 TreeBlockSync{});
             if (L == 0) {
                 for (int i = threadIdx.x; i < a.top_p; i += kTreeCThreads) {
                     a.picks[(int64_t)r * a.top_p + i] = i < kept ? key_bucket(best[i]) : -1;
@@ -323,11 +424,44 @@ __global__ void __launch_bounds__(kTreeCThreads) tree_cluster_kernel(const TreeC
                         a.pick_keys[(int64_t)r * a.top_p + i] = key;
                     }
                 }
+                if (a.lists) {  // the expansion of the picks (best[0, kept); the rest read as -1)
+                    __shared__ int scan_smem[33];
+                    const int P = a.top_p, cap = a.cap, total = P * cap;
+                    int* mem = reinterpret_cast<int*>(reinterpret_cast<char*>(csm) + a.stage_off);
+                    int* gather = mem + ((total + 3) & ~3);
+                    auto bucket = [&](int pk) -> int64_t {
+                        const int64_t b = pk < kept ? (int64_t)key_bucket(best[pk]) : -1;
+                        return b >= 0 && b < a.member_rows ? b : -1;
+                    };
+                    if (a.vec16) {
+                        const int q4 = cap / 4;
+                        for (int i = threadIdx.x; i < P * q4; i += kTreeCThreads) {
+                            const int pk = i / q4, piece = i - pk * q4;
+                            const int64_t b = bucket(pk);
+                            int* dst = mem + pk * cap + piece * 4;
+                            if (b >= 0) cp_async16(smem_u32(dst), a.members + b * cap + piece * 4, 16);
+                            else *reinterpret_cast<int4*>(dst) = make_int4(-1, -1, -1, -1);
+                        }
+                        cp_async_wait_all();
+                    } else {
+                        for (int i = threadIdx.x; i < total; i += kTreeCThreads) {
+                            const int pk = i / cap;
+                            const int64_t b = bucket(pk);
+                            mem[i] = b >= 0 ? a.members[b * cap + (i - pk * cap)] : -1;
+                        }
+                    }
+                    __syncthreads();
+                    const int width = a.top_k + a.window + a.sink;
+                    expand_walk<kTreeCThreads>(mem, total, pos, a.window, a.sink, a.top_k,
+                                               a.lists + (int64_t)r * width, width, a.lengths + r, scan_smem,
+                                               (int)threadIdx.x, TreeBlockSync{}, gather);
+                }
                 return;
             }
             const int S = (int)a.size;
+            const int64_t* kept_keys = all_kept ? keys : best;
             for (int i = threadIdx.x; i < kept * S; i += kTreeCThreads)
-                carried[i] = (int32_t)a.lk[L - 1][(int64_t)key_bucket(best[i / S]) * S + (i % S)];
+                carried[i] = (int32_t)a.lk[L - 1][(int64_t)key_bucket(kept_keys[i / S]) * S + (i % S)];
         }
         carried_n = kept * (int)a.size;
         // the leader's carried list (and its finished reads of the keys) before the next scores
@@ -362,6 +496,15 @@ static TreePlan plan_tree(int64_t R, int64_t n_built, const int64_t* level_count
     p.counters = R + 1;
     return p;
 }
+
+// The expansion a tree select may finish with (lsa_tree_select_lists).
+struct TreeWalk {
+    const int32_t* members;
+    int64_t member_rows, cap, window, sink, top_k;
+    int32_t* lists;
+    int32_t* lengths;
+};
+constexpr int64_t kTreeWalkSmem = 128 * 1024;  // staged member slots + gathered list, bytes
 
 }  // namespace lsa
 
@@ -398,12 +541,16 @@ int lsa_tree_select(const float* q, int64_t R, int64_t d, const int32_t* positio
                                 scratch, scratch_bytes, counters, n_counters, stream);
 }
 
-int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
-                         int64_t rows, int64_t n_built, const float* const* level_centroids,
-                         const int64_t* const* level_children, const int64_t* level_counts,
-                         const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
-                         int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
-                         int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream) {
+// The beam (and, with walk, the expansion when the one-launch cluster form takes the call:
+// *walked tells the caller whether the lists are written).
+static int tree_select_run(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                           int64_t rows, int64_t n_built, const float* const* level_centroids,
+                           const int64_t* const* level_children, const int64_t* level_counts,
+                           const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                           int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
+                           int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream,
+                           const TreeWalk* walk, bool* walked) {
+    if (walked) *walked = false;
     if (col_offset < 0 || col_offset + rows > INT32_MAX) return LSA_ERR_ARG;
     if (d <= 0 || d % 8 || d > 2048 || ((uintptr_t)q & 15) || top_level > kTreeMaxLevels || n_built > top_level)
         return LSA_ERR_ARG;
@@ -441,8 +588,24 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
         }
         c.bc = bucket_centroids; c.picks = picks; c.pick_keys = pick_keys; c.col_offset = col_offset;
         c.cand_cap = p.cand_cap; c.carry_cap = p.carry_cap; c.status = counters + R;
+        c.members = nullptr; c.member_rows = 0; c.cap = 0; c.window = 0; c.sink = 0; c.top_k = 0; c.vec16 = 0;
+        c.stage_off = 0; c.lists = nullptr; c.lengths = nullptr;
+        int64_t staged = 0;  // bytes of the walk's shared memory (0: no walk in this launch)
+        if (walk) {
+            const int64_t slots = top_p * walk->cap;
+            const int64_t bytes = ((slots + 3) / 4 * 4 + walk->top_k) * 4;
+            if (slots < (1 << 30) && bytes <= kTreeWalkSmem) {
+                staged = bytes;
+                c.members = walk->members; c.member_rows = walk->member_rows; c.cap = (int)walk->cap;
+                c.window = (int)walk->window; c.sink = (int)walk->sink; c.top_k = (int)walk->top_k;
+                c.vec16 = walk->cap % 4 == 0 && ((uintptr_t)walk->members & 15) == 0;
+                c.lists = walk->lists; c.lengths = walk->lengths;
+            }
+        }
         const int Kc = 32 * ckw;
-        const int csmem = (int)(p.cand_cap * 8 + (kTreeCWarps + 1) * Kc * 8 + ((p.carry_cap + 3) / 4) * 16);
+        const int base = (int)(p.cand_cap * 8 + (kTreeCWarps + 1) * Kc * 8 + ((p.carry_cap + 3) / 4) * 16);
+        c.stage_off = (base + 15) / 16 * 16;
+        const int csmem = staged ? c.stage_off + (int)staged : base;
         int most = p.cand_cap;  // scoring warps the widest level can use
         int cs = (most + kTreeCWarps * 2 - 1) / (kTreeCWarps * 2);
         if (cs < 1) cs = 1;
@@ -466,7 +629,9 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
                 return LSA_ERR_CUDA;
             if (cs > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
                 return LSA_ERR_CUDA;
-            return cudaLaunchKernelEx(&lc, kern, c) == cudaSuccess ? LSA_OK : LSA_ERR_CUDA;
+            if (cudaLaunchKernelEx(&lc, kern, c) != cudaSuccess) return LSA_ERR_CUDA;
+            if (walked) *walked = staged > 0;
+            return LSA_OK;
         };
 #define LSA_TC_KW(CH)                                               \
     do {                                                            \
@@ -533,6 +698,45 @@ int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* po
         cur ^= 1;
     }
     return LSA_OK;
+}
+
+int lsa_tree_select_keys(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                         int64_t rows, int64_t n_built, const float* const* level_centroids,
+                         const int64_t* const* level_children, const int64_t* level_counts,
+                         const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                         int64_t top_p, int32_t* picks, int64_t* pick_keys, int64_t col_offset, void* scratch,
+                         int64_t scratch_bytes, int32_t* counters, int64_t n_counters, cudaStream_t stream) {
+    return tree_select_run(q, R, d, positions, block, bpb, rows, n_built, level_centroids, level_children,
+                           level_counts, bucket_centroids, size, nb, top_level, beam, top_p, picks, pick_keys,
+                           col_offset, scratch, scratch_bytes, counters, n_counters, stream, nullptr, nullptr);
+}
+
+int lsa_expand_in_order(const int32_t* picked, int64_t R, int64_t P, int64_t ldp, const int32_t* members,
+                        int64_t member_rows, int64_t cap, const int32_t* positions, int64_t window, int64_t sink,
+                        int64_t top_k, int32_t* lists, int32_t* lengths, cudaStream_t stream);
+
+// The beam's picks and their expansion into read lists: one launch when the cluster form
+// takes the rows and the staged members fit its shared memory, else the beam then the
+// expansion kernel - the same lists either way.
+int lsa_tree_select_lists(const float* q, int64_t R, int64_t d, const int32_t* positions, int64_t block, int64_t bpb,
+                          int64_t rows, int64_t n_built, const float* const* level_centroids,
+                          const int64_t* const* level_children, const int64_t* level_counts,
+                          const float* bucket_centroids, int64_t size, int64_t nb, int64_t top_level, int64_t beam,
+                          int64_t top_p, const int32_t* members, int64_t member_rows, int64_t cap, int64_t window,
+                          int64_t sink, int64_t top_k, int32_t* picks, int32_t* lists, int32_t* lengths,
+                          void* scratch, int64_t scratch_bytes, int32_t* counters, int64_t n_counters,
+                          cudaStream_t stream) {
+    if (!members || !picks || !lists || !lengths || cap <= 0 || member_rows < 0 || window < 0 || sink < 0 ||
+        top_k < 0)
+        return LSA_ERR_ARG;
+    TreeWalk w{members, member_rows, cap, window, sink, top_k, lists, lengths};
+    bool walked = false;
+    int rc = tree_select_run(q, R, d, positions, block, bpb, rows, n_built, level_centroids, level_children,
+                             level_counts, bucket_centroids, size, nb, top_level, beam, top_p, picks, nullptr, 0,
+                             scratch, scratch_bytes, counters, n_counters, stream, &w, &walked);
+    if (rc != LSA_OK || walked || R == 0) return rc;
+    return lsa_expand_in_order(picks, R, top_p, top_p, members, member_rows, cap, positions, window, sink, top_k,
+                               lists, lengths, stream);
 }
 
 }  // extern "C"

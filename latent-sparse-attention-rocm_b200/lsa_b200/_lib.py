@@ -85,6 +85,8 @@ SIGNATURES = {
     "lsa_tree_plan": (_INT, [_I, _I, _P, _I, _I, _I, _I, _I, _P, _P]),
     "lsa_tree_select": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _I, _P,
                                _I, _P]),
+    "lsa_tree_select_lists": (_INT, [_P, _I, _I, _P, _I, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _I,
+                                     _I, _I, _I, _P, _P, _P, _P, _I, _P, _I, _P]),
 }
 
 
