@@ -132,3 +132,27 @@ def test_torch_ops_load_first_in_a_fresh_process():
             "print(_lib.torch_ops().sparse_read)" % str(ROOT / "latent-sparse-attention-rocm_b200"))
     res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
     assert res.returncode == 0 and "lsa.sparse_read" in res.stdout, res.stderr[-2000:]
+
+
+def test_tree_lists_refuses_missing_buffers_before_any_cuda_call():
+    """lsa_tree_select_lists checks its expansion arguments first: a null member table or
+    output, or a negative window, returns LSA_ERR_ARG (-1) without touching the GPU."""
+    import ctypes
+
+    from lsa_b200 import _lib
+
+    try:
+        L = _lib.lib()
+    except OSError as e:
+        pytest.skip(f"CUDA runtime not loadable here: {e}")
+    one = (ctypes.c_int64 * 1)(1)
+    ptrs = (ctypes.c_void_p * 1)(None)
+    buf = ctypes.c_void_p(16)  # never dereferenced: the call returns before any use
+
+    def call(members, lists, window):
+        return L.lsa_tree_select_lists(buf, 1, 64, buf, 512, 8, 8, 1, ptrs, ptrs, one, buf, 4, 64, 3, 64, 32,
+                                       members, 8, 64, window, 4, 2048, buf, lists, buf, buf, 1 << 20, buf, 2, None)
+
+    assert call(None, buf, 64) == -1
+    assert call(buf, None, 64) == -1
+    assert call(buf, buf, -1) == -1
