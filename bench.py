@@ -975,6 +975,8 @@ def run_tree1m(args, rank, world, dev, dump=None):
 
     def step(which):  # all sequences' candidates in one all-gather, one partial read, all partials in a second
         q, k, v, iq, shards = sets[which]
+        if world == 1:  # one GPU holds every sequence whole: nothing to exchange
+            return seqshard.one_shard_decode_batch(q, k, v, iq, pos, shards, pcfg, scale)
         return seqshard.seqshard_decode_batch(q, k, v, iq, pos, shards, pcfg, gather, scale)
 
     for _ in range(args.warmup):
@@ -1032,7 +1034,7 @@ def run_tree1m(args, rank, world, dev, dump=None):
         "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded drift keys, N(0,1) q/v)",
         "config": {"workload": "tree1m", "batch": B, "context": C, "heads_q": HQ, "heads_kv": HKV, "head_dim": DH,
-                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": f"{exchange} all-gather x2/step (candidates, partials)",
+                   "shard_tokens": n, "parallelism": f"sequence-shard{world}", "exchange": f"{exchange} all-gather x2/step (candidates, partials)" if world > 1 else "none (one shard: the one-launch tree select per sequence, one read)",
                    "cuda_graph": use_graph, "rotation": "2 query/cache sets alternate step by step",
                    **{k2: TREE_CFG[k2] for k2 in ("bucket_size", "top_p", "top_k", "beam_width")},
                    "l2": "no flush: 2 sets of 4 x 1M-token caches (32 GiB) >> L2, consecutive steps read different sets"},

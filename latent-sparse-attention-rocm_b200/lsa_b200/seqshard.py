@@ -247,6 +247,27 @@ def _fan_out(fns, device):
     return out
 
 
+def one_shard_decode_batch(q, k, v, index_queries, positions, shards, config, scale=None):
+    """``seqshard_decode_batch`` when one GPU holds every sequence whole (a single shard that
+    starts at position 0): there is nothing to exchange, so each sequence's read lists come
+    from its one-launch tree select (the beam and the expansion, ``lsa_tree_select_lists``;
+    a side stream each) and one read covers all sequences. The lists equal the sharded
+    procedure's with one shard (the beam's visible count is clamped to the shard's buckets
+    either way); the output is one read instead of a partial read and a log-sum-exp merge,
+    equal within the read's tolerance. Shapes as ``seqshard_decode_batch``."""
+    B = len(shards)
+    if q.shape[0] != B or k.shape[0] != B or v.shape[0] != B:
+        raise ValueError("one_shard_decode_batch: one q / k / v batch row per shard index")
+    if any(s.start != 0 or s.length != k.shape[1] for s in shards):
+        raise ValueError("one_shard_decode_batch: every shard must hold its whole sequence from position 0")
+    dev = q.device
+    walks = _fan_out([lambda b=b: pipeline.tree_select(index_queries[b], positions, shards[b].buckets,
+                                                       shards[b].hierarchy, config) for b in range(B)], dev)
+    lists = torch.stack([w[0] for w in walks])
+    lengths = torch.stack([w[1] for w in walks])
+    return pipeline.lsa_read(q, k, v, lists, lengths, scale)
+
+
 def seqshard_decode_batch(q, k, v, index_queries, positions, shards, config, gather, scale=None):
     """One decode step of several sharded sequences with TWO exchanges in all: the candidate
     keys of every sequence in one all-gather, the partial outputs and log2-sum-exps of every

@@ -155,3 +155,39 @@ def test_batched_step_in_cuda_graph(lsa, oracle):
         stream.synchronize()
         assert torch.equal(out, eager2) and not torch.equal(eager2, eager)
     del g
+
+
+def test_one_shard_batch_equals_the_sharded_step(lsa, oracle):
+    """With one GPU holding every sequence whole, one_shard_decode_batch (the one-launch tree
+    select per sequence, one read) matches the sharded step with one rank within the read
+    tolerance, eagerly and replayed from a CUDA graph (byte for byte against its own eager
+    output)."""
+    from lsa_b200 import seqshard
+
+    C = 16384
+    seqs = [_setup(lsa, oracle, C, 1, seed=s) for s in (41, 42, 43)]
+    pos = torch.tensor([C - 1], dtype=torch.int32, device=DEV)
+    pcfg = seqs[0][4]
+    q = torch.cat([s[0] for s in seqs])
+    k = torch.cat([s[1] for s in seqs])
+    v = torch.cat([s[2] for s in seqs])
+    iqs = [s[3] for s in seqs]
+    shards = [s[6][0] for s in seqs]
+    want = seqshard.seqshard_decode_batch(q, k, v, iqs, pos, shards, pcfg, lambda x: x[None])
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        step = lambda: seqshard.one_shard_decode_batch(q, k, v, iqs, pos, shards, pcfg)
+        eager = step().clone()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            out = step()
+        g.replay()
+        stream.synchronize()
+        assert torch.equal(out, eager)
+    del g
+    assert eager.shape == want.shape
+    assert float((eager.float() - want.float()).abs().max()) <= 2e-2
+    with pytest.raises(ValueError):  # a shard that does not start at position 0 is not a whole sequence
+        bad = seqshard.ShardIndex(1024, shards[0].length, shards[0].buckets, shards[0].hierarchy, 0)
+        seqshard.one_shard_decode_batch(q[:1], k[:1], v[:1], iqs[:1], pos, [bad], pcfg)
