@@ -117,3 +117,25 @@ def test_shard_bounds_block_aligned():
             assert a1 == b0 and a0 % block == 0
     with pytest.raises(ValueError):
         shard_bounds(100, 2, 2, 64)
+
+
+def test_one_shard_batch_refuses_partial_shards_on_cpu():
+    """one_shard_decode_batch serves a GPU that holds every sequence whole: a shard that starts
+    past position 0, one shorter than the cache, or a batch without one shard per sequence is
+    refused before any kernel runs."""
+    sys.path.insert(0, os.path.join(ROOT, "latent-sparse-attention-rocm_b200"))
+    import torch
+
+    from lsa_b200 import pipeline
+    from lsa_b200.seqshard import ShardIndex, one_shard_decode_batch
+
+    q = torch.zeros(1, 1, 8, 64)
+    k = torch.zeros(1, 2048, 2, 64)
+    cfg = pipeline.PortConfig()
+    whole = ShardIndex(0, 2048, None, None, 0)
+    late = ShardIndex(1024, 1024, None, None, 0)
+    short = ShardIndex(0, 1024, None, None, 0)
+    pos = torch.tensor([2047], dtype=torch.int32)
+    for shards in ([late], [short], [whole, whole]):
+        with pytest.raises(ValueError):
+            one_shard_decode_batch(q, k, k, [q[0, :, :2].reshape(1, -1)], pos, shards, cfg)
